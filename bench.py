@@ -1,0 +1,387 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 block-local attention path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2] [--halo 1]
+    python bench.py --impl reference ...      # the reference's CPU algorithm
+
+A step is one forward pass of block-local attention over one batch of the
+workload (default c2: batch 32, 12 heads, seq 1024, head_dim 64, block 64,
+Block3 = halo 1, valid lengths U[512, 1024], N(0,1) inputs from seed 1).
+Under torchrun every rank owns its own batch of 32 sequences of a global
+batch of 32*N (batch x heads is the shard; no collective on the data path):
+weak scaling.  `value` is whole-job algorithmic GFLOP/s (4 * head_dim FLOPs
+per allowed query/key pair, counted exactly), timed with CUDA events over K
+steps, max over ranks.  `e2e` is the same metric through the host-buffer API
+(raya_attn_forward_host: pinned host inputs -> device -> kernel -> host
+output, synchronous), wall-clock, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 2**20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", default="c2")
+    ap.add_argument("--halo", type=int, default=1)
+    ap.add_argument("--kernel", type=int, default=0, help="0 auto, 1 tiled64, 2 rowwise")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="target CPU work of the cpu_baseline sample")
+    return ap.parse_args()
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_ids):
+        self.gpu_ids = gpu_ids
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", ",".join(str(g) for g in self.gpu_ids)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def load_peaks() -> dict:
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        return {}
+
+
+def load_traffic(key: str):
+    """DRAM bytes per launch from a committed ncu summary, if any."""
+    try:
+        t = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
+        return t.get(key)
+    except (OSError, ValueError):
+        return None
+
+
+# ---------------------------------------------------------------- reference arm
+
+def run_reference(args) -> None:
+    """The reference's algorithm on the host cores: the C restatement of
+    raya's Tiled kernel with its AVX2+FMA micro-kernels (oracle/tiled.c), all
+    host threads, on the workload of the B200 arm.  The reference itself is
+    Rust and cannot be built here (no cargo/rustc)."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import oracle
+    from raya_b200.workloads import CONFIGS
+
+    w = CONFIGS[args.workload].with_halo(args.halo)
+    threads = host_threads()
+    valid = w.valid_len()
+    p = oracle.Problem(w.batch, w.heads, w.seq, w.head_dim, mask=oracle.MASK_BLOCK,
+                       block=w.block, halo=w.halo)
+    # Bounded sample of the workload: whole (batch entry) slices, sized so a
+    # step is ~2 s at an assumed 100 GFLOP/s; inputs N(0, stddev^2) on the host.
+    pairs_all, _ = oracle.count(p, valid)
+    per_b = pairs_all / w.batch * 4 * w.head_dim
+    nb = max(1, min(w.batch, int(2.0 * 100e9 / max(per_b, 1.0))))
+    ps = oracle.Problem(nb, w.heads, w.seq, w.head_dim, mask=oracle.MASK_BLOCK, block=w.block,
+                        halo=w.halo)
+    rng = np.random.default_rng(w.seed)
+    q, k, v = (rng.standard_normal(ps.numel, dtype=np.float32) * np.float32(w.stddev) for _ in range(3))
+    out = np.zeros(ps.numel, dtype=np.float32)
+    vs = valid[:nb]
+    pairs, rows = oracle.count(ps, vs)
+    for _ in range(args.warmup):
+        oracle.tiled(ps, q, k, v, vs, threads=threads, out=out)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.tiled(ps, q, k, v, vs, threads=threads, out=out)
+    dt = (time.perf_counter() - t0) / args.steps
+    gflops = 4 * w.head_dim * pairs / dt / 1e9
+    sample = (f"{nb} of {w.batch} sequences x {w.heads} heads of {w.name} (halo {w.halo}) per step, "
+              f"N(0,{w.stddev}^2) host inputs")
+    line = {
+        "metric": "block-local attn GFLOP/s", "value": round(gflops, 3), "unit": "GFLOP/s",
+        "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(w, world),
+        "queries_per_s": round(rows / dt, 1),
+        "cpu_baseline": {"value": round(gflops, 3), "unit": "GFLOP/s", "cores": threads,
+                         "kind": "port", "sample": sample, "cpu": cpu_model(),
+                         "what": "C restatement of raya Tiled + AVX2 micro-kernels (oracle/tiled.c)"},
+        "e2e": {"value": round(gflops, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(w, world: int) -> dict:
+    return {"workload": f"{w.name}: batch {w.batch}/GPU x {w.heads} heads x seq {w.seq} x d {w.head_dim},"
+                        f" block {w.block}, halo {w.halo} ({'Block3' if w.halo == 1 else 'own block'}),"
+                        f" valid {w.valid or 'full'}, seed {w.seed}, N(0,{w.stddev}^2)",
+            "global_batch": w.batch * world, "seq_len": w.seq, "heads": w.heads,
+            "head_dim": w.head_dim, "block": w.block, "halo": w.halo,
+            "parallelism": f"batch x heads sharded over {world} GPU(s), no collective",
+            "l2": f"inputs+output {4 * w.numel * 4 / 2**20:.0f} MiB per GPU > 126 MiB L2 (no flush)"}
+
+
+# ---------------------------------------------------------------- B200 arm
+
+def run_b200(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import raya_b200 as rb
+    from raya_b200.workloads import CONFIGS, fill_device
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    w = CONFIGS[args.workload].with_halo(args.halo)
+    D = w.head_dim
+    # This rank's batch entries: [rank*B, (rank+1)*B) of the global batch.
+    b0 = rank * w.batch
+    valid = w.valid_len(first=b0)
+    shape = rb.AttnShape(heads=w.heads, seq=w.seq, head_dim=D, batch=w.batch)
+    params = rb.AttnParams.new(rb.Mask.block(w.halo), valid, D, block=w.block)
+    pairs, rows = rb.work(shape, params)
+    n = w.numel
+    q, k, v, out = (torch.empty(n, dtype=torch.float32, device=dev) for _ in range(4))
+    fill_device(w, (q, k, v), bh0=b0 * w.heads)
+    dvalid = torch.from_numpy(valid).to(dev)
+    kern = rb.Cuda(rb.CudaConfig(device=local, kernel=args.kernel))
+    stream = torch.cuda.current_stream(dev)
+
+    # Live FFMA peak of this GPU (the roofline denominator: no FP32 figure is
+    # in MEASURED_PEAKS.json), measured before the timed region.
+    ffma_tflops = rb.ffma_peak(5)
+
+    def step():
+        kern.attend_device(shape, params, q, k, v, out, valid_len=dvalid, stream=stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    rb.sync_status(stream)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(list(range(world)) if rank == 0 else [local])
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    clocks = sampler.stop() if rank == 0 else None
+    rb.sync_status(stream)
+    if world > 1:
+        t = torch.tensor([ms, float(pairs), float(rows)], dtype=torch.float64, device=dev)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        ms_max, pairs_all, rows_all = float(mx[0]), float(t[1]), float(t[2])
+    else:
+        ms_max, pairs_all, rows_all = ms, float(pairs), float(rows)
+    flops_all = 4.0 * D * pairs_all
+    gflops = flops_all / (ms_max * 1e-3) / 1e9
+    qps = rows_all / (ms_max * 1e-3)
+
+    # Roofline of the one kernel of a step (per launch on this rank).
+    flops_launch = 4.0 * D * pairs
+    bytes_launch = 4.0 * D * (3 * float(valid.sum()) + w.batch * w.seq) * w.heads
+    achieved_tf = flops_launch / (ms * 1e-3) / 1e12
+    peaks = load_peaks()
+    hbm = peaks.get("hbm_gbs")
+    tkey = f"{w.name}-halo{w.halo}"
+    roofline = {"bound": "ffma", "achieved": round(achieved_tf, 3), "peak": round(ffma_tflops, 3),
+                "unit": "TFLOP/s", "frac": round(achieved_tf / ffma_tflops, 4),
+                "peak_source": "measured live: raya_attn_ffma_peak (FP32 FFMA probe, this GPU)",
+                "nominal_peak": round(148 * 128 * 2 * 1.965e9 / 1e12, 1),
+                "traffic": load_traffic(tkey),
+                "algorithmic_bytes": bytes_launch,
+                "hbm": {"achieved": round(bytes_launch / (ms * 1e-3) / 1e9, 1), "peak": hbm,
+                        "unit": "GB/s", "frac": round(bytes_launch / (ms * 1e-3) / 1e9 / hbm, 4) if hbm else None,
+                        "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if hbm else None}}
+
+    # End to end through the host-buffer API (pinned inputs, synchronous).
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv, ho = (torch.empty(n, dtype=torch.float32).pin_memory() for _ in range(4))
+        for h, d in zip((hq, hk, hv), (q, k, v)):
+            h.copy_(d)
+        hq_np, hk_np, hv_np, ho_np = (x.numpy() for x in (hq, hk, hv, ho))
+        kern.attend(shape, params, hq_np, hk_np, hv_np, ho_np)  # warm-up (staging buffers)
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            kern.attend(shape, params, hq_np, hk_np, hv_np, ho_np)
+        e2e_s = (time.perf_counter() - t0) / args.e2e_steps
+        if world > 1:
+            t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t[0])
+        e2e = {"value": round(flops_all / e2e_s / 1e9, 3), "unit": "GFLOP/s",
+               "ms_per_step": round(e2e_s * 1e3, 3),
+               "h2d_bytes_per_step": 3 * n * 4 + w.batch * 4, "d2h_bytes_per_step": n * 4,
+               "api": "raya_attn_forward_host (AttentionKernel::attend contract), pinned host buffers"}
+        # the host call must agree with the device call bit for bit
+        assert torch.equal(ho, out.cpu()), "host-buffer call differs from the device call"
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args, w, q, k, v, valid, dev)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": "block-local attn GFLOP/s", "value": round(gflops, 3), "unit": "GFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), device-generated)",
+        "config": workload_config(w, world),
+        "queries_per_s": round(qps, 1),
+        "frac_fp32_peak": roofline["frac"],
+        "gpu_launches": args.steps,
+        "kernel": "tiled64 (raya_b200/csrc/tiled64.cuh)" if args.kernel in (0, 1) else "rowwise",
+        "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(args, w, q, k, v, valid, dev) -> dict:
+    """The oracle's Tiled+AVX2 restatement on the host cores over a bounded
+    sample (whole sequences) of the same device-generated inputs."""
+    import torch
+
+    import oracle
+
+    threads = host_threads()
+    D, L, H = w.head_dim, w.seq, w.heads
+    p_all = oracle.Problem(w.batch, H, L, D, mask=oracle.MASK_BLOCK, block=w.block, halo=w.halo)
+    pairs_all, _ = oracle.count(p_all, valid)
+    # calibrate on one sequence, then size the sample to ~cpu_seconds
+    def run(nb):
+        ps = oracle.Problem(nb, H, L, D, mask=oracle.MASK_BLOCK, block=w.block, halo=w.halo)
+        m = nb * H * L * D
+        qs, ks, vs = (x[:m].cpu().numpy() for x in (q, k, v))
+        t0 = time.perf_counter()
+        oracle.tiled(ps, qs, ks, vs, valid[:nb], threads=threads)
+        dt = time.perf_counter() - t0
+        pairs, _ = oracle.count(ps, valid[:nb])
+        return 4 * D * pairs / dt / 1e9, dt
+    rate, dt1 = run(1)
+    nb = int(max(1, min(w.batch, args.cpu_seconds / max(dt1, 1e-3))))
+    rate, dt = run(nb)
+    return {"value": round(rate, 3), "unit": "GFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{nb} of {w.batch} sequences x {H} heads of {w.name} (same inputs), {dt:.1f} s",
+            "cpu": cpu_model(),
+            "what": "C restatement of raya Tiled + AVX2 micro-kernels (oracle/tiled.c)"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,161 @@
+/*
+ * raya_attn.h — C ABI of the B200 (sm_100a) block-local attention library
+ * (libraya_attn.so).  Plain pointers and sizes only: no CUDA or torch types
+ * appear in these signatures (streams are passed as `void*` holding a
+ * cudaStream_t, NULL meaning the legacy default stream).
+ *
+ * It replaces raya's `AttentionKernel` implementations for the block-local
+ * path (paths relative to the raya project root):
+ *   trait AttentionKernel::attend   crates/raya-kernels/src/attention.rs:113-125
+ *   validate                        crates/raya-kernels/src/attention.rs:128-170
+ *   Tiled::attend                   crates/raya-kernels/src/tiled/mod.rs:138-149
+ * A Rust maintainer binds `raya_attn_forward_host` with `batch = 1` inside an
+ * `impl AttentionKernel for Cuda` (the binding is shown in INTEGRATION.md).
+ *
+ * Layout contract (attention.rs:72-78, extended with a batch dimension):
+ * q, k, v and out are row-major fp32 `[batch][heads][seq][head_dim]`; the
+ * reference's `[heads][seq][head_dim]` is batch = 1.  valid_len holds one
+ * int32 per batch entry: keys at or beyond it are padding and query rows at
+ * or beyond it are written as +0.0f.  `out` is fully overwritten.
+ *
+ * Semantics (attention.rs:108-112, naive.rs:13-65): for row i < valid_len,
+ * out[i] = sum_j softmax_j(scale * q_i . k_j) v_j over keys j < valid_len
+ * allowed by the mask; rows with no allowed key are zero.
+ */
+#ifndef RAYA_ATTN_H
+#define RAYA_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RAYA_ATTN_VERSION 1
+
+/* Mirrors KernelError (attention.rs:8-20) plus device-side failures. */
+typedef enum {
+  RAYA_ATTN_OK = 0,
+  RAYA_ATTN_ERR_SHAPE = 1,       /* KernelError::Shape */
+  RAYA_ATTN_ERR_LENGTH = 2,      /* KernelError::Length { name, got, expected } */
+  RAYA_ATTN_ERR_UNSUPPORTED = 3, /* KernelError::Unsupported */
+  RAYA_ATTN_ERR_CUDA = 4,        /* a CUDA runtime call failed */
+  RAYA_ATTN_ERR_TIMEOUT = 5,     /* a device-side wait gave up (bounded spin) */
+  RAYA_ATTN_ERR_NCCL = 6         /* reserved for collective failures */
+} raya_attn_status;
+
+/* Mask kinds (attention.rs:22-35, generalised):
+ *   BLOCK  : |i/block - j/block| <= halo.  halo = 1, block = 128 is
+ *            Mask::Block3 (Laya's block_local); halo = 0 is "own block only".
+ *   WINDOW : |i - j| <= window.  window = 64 is Mask::Window64, any other
+ *            value is Mask::Sliding(window).
+ *   FULL   : every key below valid_len (Mask::Full).                       */
+typedef enum {
+  RAYA_MASK_BLOCK = 0,
+  RAYA_MASK_WINDOW = 1,
+  RAYA_MASK_FULL = 2
+} raya_mask_kind;
+
+/* AttnShape + AttnParams (attention.rs:72-106) with a batch dimension.
+ * Rust's `AttnParams::new` sets scale = 1/sqrt(head_dim) in f32. */
+typedef struct {
+  int64_t batch;    /* >= 1 */
+  int64_t heads;    /* >= 1 */
+  int64_t seq;      /* >= 0 */
+  int64_t head_dim; /* >= 8, multiple of 8 (validate), <= 256 (this library) */
+  int64_t block;    /* BLOCK masks: block size, >= 1 (reference: only 128) */
+  int32_t mask;     /* raya_mask_kind */
+  int32_t halo;     /* BLOCK masks: key blocks on each side, >= 0 */
+  int64_t window;   /* WINDOW masks: half width, >= 0 */
+  float scale;      /* softmax scale applied to q.k */
+} raya_attn_desc;
+
+/* Kernel selection for raya_attn_forward_ex (tests and benchmarks). */
+typedef enum {
+  RAYA_KERNEL_AUTO = 0,     /* tiled FFMA kernel when head_dim == 64, else rowwise */
+  RAYA_KERNEL_TILED64 = 1,  /* 128-row CTA tiles, TMA-staged 64-key tiles, head_dim 64 */
+  RAYA_KERNEL_ROWWISE = 2   /* one warp per query row, any head_dim */
+} raya_kernel_id;
+
+/* Argument checks of validate (attention.rs:128-170), extended to the batch
+ * layout.  Buffer lengths are element counts, like the Rust slices' len();
+ * valid_len is a HOST array of `batch` entries or NULL (every sequence fully
+ * valid).  Returns OK or the error the reference would raise; the message is
+ * available from raya_attn_last_error(). */
+raya_attn_status raya_attn_validate(const raya_attn_desc* desc, const int32_t* valid_len,
+                                    size_t q_len, size_t k_len, size_t v_len,
+                                    size_t out_len);
+
+/* Synchronous host-buffer call: the AttentionKernel::attend contract
+ * (attention.rs:113-125, tiled/mod.rs:138-149).  q, k, v, out and valid_len
+ * are HOST pointers (pageable or pinned).  Validates, copies the inputs to
+ * device `device`, runs the kernel, copies `out` back and synchronises.
+ * Thread-safe: concurrent callers serialise on the device's staging buffers. */
+raya_attn_status raya_attn_forward_host(const raya_attn_desc* desc, const float* q,
+                                        size_t q_len, const float* k, size_t k_len,
+                                        const float* v, size_t v_len, float* out,
+                                        size_t out_len, const int32_t* valid_len,
+                                        int device);
+
+/* Asynchronous device-buffer call on `stream` (the B200-native entry point,
+ * no reference counterpart beyond the trait's semantics).  q, k, v, out are
+ * DEVICE pointers holding batch*heads*seq*head_dim floats; valid_len is a
+ * DEVICE array of `batch` int32 or NULL.  The shape is validated on the host;
+ * valid_len values are not visible to the host here, so the kernel clamps
+ * each into [0, seq] (use raya_attn_validate on a host copy for the
+ * reference's error).  Launch errors are returned; device-side timeouts are
+ * reported by raya_attn_sync_status.  Allocates nothing. */
+raya_attn_status raya_attn_forward(const raya_attn_desc* desc, const float* q,
+                                   const float* k, const float* v, float* out,
+                                   const int32_t* valid_len, void* stream);
+
+/* raya_attn_forward with an explicit kernel (raya_kernel_id). */
+raya_attn_status raya_attn_forward_ex(const raya_attn_desc* desc, const float* q,
+                                      const float* k, const float* v, float* out,
+                                      const int32_t* valid_len, void* stream,
+                                      int kernel_id);
+
+/* Synchronises `stream` and returns RAYA_ATTN_ERR_TIMEOUT if any kernel of
+ * this library on the current device recorded a bounded-wait timeout since
+ * the last call (the record is then cleared), RAYA_ATTN_ERR_CUDA on a CUDA
+ * error, else OK. */
+raya_attn_status raya_attn_sync_status(void* stream);
+
+/* Message of the last error raised on the calling thread (KernelError's
+ * Display text for the reference's errors).  Never NULL. */
+const char* raya_attn_last_error(void);
+
+/* Exact algorithmic work of one call: allowed (query < valid, key < valid,
+ * mask-allowed) pairs and valid query rows, summed over batch and heads.
+ * valid_len is a HOST array or NULL.  FLOPs = 4 * head_dim * pairs. */
+raya_attn_status raya_attn_work(const raya_attn_desc* desc, const int32_t* valid_len,
+                                uint64_t* pairs, uint64_t* valid_rows);
+
+/* Multi-GPU partition (batch x heads is the shard): the contiguous range
+ * [*bh_begin, *bh_end) of flattened batch*heads slices that `rank` of
+ * `world` owns, balanced by allowed-pair count.  valid_len is a HOST array or
+ * NULL.  Every rank computes the same partition; ranges tile [0, batch*heads). */
+raya_attn_status raya_attn_shard(const raya_attn_desc* desc, const int32_t* valid_len,
+                                 int world, int rank, int64_t* bh_begin, int64_t* bh_end);
+
+/* Fills DEVICE buffer dst[0..n) with seeded N(0, stddev^2) values:
+ * splitmix64 of (seed, stream_id, pair index) -> two 24-bit uniforms ->
+ * Box-Muller.  Element i is a function of (seed, stream_id, first_index + i)
+ * only, so shards of a larger tensor can be generated independently. */
+raya_attn_status raya_attn_fill_normal(float* dst, int64_t n, uint64_t seed,
+                                       uint32_t stream_id, int64_t first_index,
+                                       float stddev, void* stream);
+
+/* FP32 FFMA throughput probe on the current device: a kernel of dependent-
+ * chain-free FFMAs over every SM, timed with CUDA events (best of `reps`).
+ * Writes the achieved FFMA rate in TFLOP/s (2 flops per FFMA). */
+raya_attn_status raya_attn_ffma_peak(int reps, double* tflops);
+
+/* Library ABI version (RAYA_ATTN_VERSION). */
+int raya_attn_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RAYA_ATTN_H */

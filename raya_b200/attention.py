@@ -1,0 +1,337 @@
+"""raya's attention contract, mirrored over the B200 library.
+
+Python restatement of crates/raya-kernels/src/attention.rs (paths relative to
+the raya project root) so that callers and tests read like the reference's:
+
+* ``BLOCK`` / ``WINDOW``                       attention.rs:3-6
+* ``KernelError`` and its three kinds          attention.rs:8-20 (plus device errors)
+* ``Mask`` with ``key_range`` / ``allows``     attention.rs:22-70 (generalised:
+  ``Mask.block(halo)``, ``Mask.sliding(w)``; ``BLOCK3`` = halo 1,
+  ``WINDOW64`` = sliding(64))
+* ``AttnShape`` / ``AttnParams``               attention.rs:72-106 (a ``batch``
+  dimension and per-sequence ``valid_len``)
+* ``AttentionKernel``                          attention.rs:108-125
+* ``validate``                                 attention.rs:127-170
+
+``Cuda`` is the drop-in kernel: ``attend`` takes host buffers like the Rust
+trait (``raya_attn_forward_host``); ``attend_device`` takes CUDA tensors that
+already live in HBM (``raya_attn_forward``).  Every compute call goes to the
+CUDA library; there is no CPU path.
+"""
+from __future__ import annotations
+
+import abc
+import ctypes
+from dataclasses import dataclass, field
+from typing import Sequence, Union
+
+import numpy as np
+
+from . import _lib
+from ._lib import Desc, lib
+
+BLOCK = 128   # attention.rs:4 — Laya's block_local block size
+WINDOW = 64   # attention.rs:6 — half width of the exact local window
+
+
+class KernelError(Exception):
+    """attention.rs:8-20.  ``str(err)`` is the reference's Display text."""
+
+
+class ShapeError(KernelError):
+    """KernelError::Shape"""
+
+
+class LengthError(KernelError):
+    """KernelError::Length { name, got, expected }"""
+
+    def __init__(self, message: str, name: str = "", got: int = 0, expected: int = 0):
+        super().__init__(message)
+        self.name, self.got, self.expected = name, got, expected
+
+
+class UnsupportedError(KernelError):
+    """KernelError::Unsupported"""
+
+
+class CudaError(KernelError):
+    """A CUDA runtime call failed (no reference counterpart)."""
+
+
+class DeviceTimeout(KernelError):
+    """A bounded device-side wait gave up (no reference counterpart)."""
+
+
+_ERRORS = {
+    _lib.ERR_SHAPE: ShapeError,
+    _lib.ERR_LENGTH: LengthError,
+    _lib.ERR_UNSUPPORTED: UnsupportedError,
+    _lib.ERR_CUDA: CudaError,
+    _lib.ERR_TIMEOUT: DeviceTimeout,
+}
+
+
+def _check(status: int, lengths: dict | None = None) -> None:
+    if status == _lib.OK:
+        return
+    msg = _lib.last_error()
+    cls = _ERRORS.get(status, KernelError)
+    if cls is LengthError:
+        # "buffer `q` has length 3, expected 32"
+        name = msg.split("`")[1] if "`" in msg else ""
+        got = lengths.get(name, 0) if lengths else 0
+        expected = int(msg.rsplit(" ", 1)[-1]) if msg[-1:].isdigit() else 0
+        raise LengthError(msg, name=name, got=got, expected=expected)
+    raise cls(msg)
+
+
+@dataclass(frozen=True)
+class Mask:
+    """Which keys a query may attend (besides ``j < valid_len``)."""
+
+    kind: int
+    param: int = 0  # halo for BLOCK masks, half width for WINDOW masks
+
+    @staticmethod
+    def block(halo: int) -> "Mask":
+        """Query block b sees key blocks b-halo ..= b+halo (halo 1 = Block3)."""
+        return Mask(_lib.MASK_BLOCK, halo)
+
+    @staticmethod
+    def sliding(w: int) -> "Mask":
+        """Exact window |i - j| <= w (w = 64 is Window64)."""
+        return Mask(_lib.MASK_WINDOW, w)
+
+    def name(self) -> str:  # attention.rs:38-45
+        if self.kind == _lib.MASK_BLOCK:
+            return "block3" if self.param == 1 else f"block{2 * self.param + 1}"
+        if self.kind == _lib.MASK_WINDOW:
+            return "window64" if self.param == WINDOW else "sliding"
+        return "full"
+
+    def key_range(self, i: int, valid_len: int, block: int = BLOCK) -> range:
+        """attention.rs:48-59 with BLOCK -> block and 1 -> halo."""
+        if self.kind == _lib.MASK_BLOCK:
+            b = i // block
+            lo, hi = max(b - self.param, 0) * block, (b + self.param + 1) * block
+        elif self.kind == _lib.MASK_WINDOW:
+            lo, hi = max(i - self.param, 0), i + self.param + 1
+        else:
+            lo, hi = 0, valid_len
+        return range(min(lo, valid_len), min(hi, valid_len))
+
+    def allows(self, i: int, j: int, block: int = BLOCK) -> bool:
+        """attention.rs:62-69, ignoring valid_len."""
+        if self.kind == _lib.MASK_BLOCK:
+            return abs(i // block - j // block) <= self.param
+        if self.kind == _lib.MASK_WINDOW:
+            return abs(i - j) <= self.param
+        return True
+
+
+Mask.BLOCK3 = Mask.block(1)
+Mask.WINDOW64 = Mask.sliding(WINDOW)
+Mask.FULL = Mask(_lib.MASK_FULL, 0)
+
+
+@dataclass(frozen=True)
+class AttnShape:
+    """Buffers are ``[batch][heads][seq][head_dim]`` row-major fp32
+    (attention.rs:72-84 is batch = 1)."""
+
+    heads: int
+    seq: int
+    head_dim: int
+    batch: int = 1
+
+    def numel(self) -> int:
+        return self.batch * self.heads * self.seq * self.head_dim
+
+
+ValidLen = Union[int, Sequence[int], np.ndarray]
+
+
+@dataclass(frozen=True)
+class AttnParams:
+    """attention.rs:86-106.  ``valid_len`` is one length for every batch
+    entry or one per batch entry."""
+
+    mask: Mask
+    block: int
+    valid_len: ValidLen
+    scale: float
+
+    @staticmethod
+    def new(mask: Mask, valid_len: ValidLen, head_dim: int, block: int = BLOCK) -> "AttnParams":
+        # attention.rs:103: 1.0 / (head_dim as f32).sqrt(), computed in f32
+        scale = float(np.float32(1.0) / np.sqrt(np.float32(head_dim)))
+        return AttnParams(mask=mask, block=block, valid_len=valid_len, scale=scale)
+
+    def valid_array(self, batch: int) -> np.ndarray:
+        v = np.asarray(self.valid_len, dtype=np.int64)
+        if v.ndim == 0:
+            v = np.full(batch, int(v), dtype=np.int64)
+        if v.shape != (batch,):
+            raise ShapeError(f"invalid shape: {v.size} valid lengths for batch {batch}")
+        if (v < -2**31).any() or (v > 2**31 - 1).any():
+            raise ShapeError("invalid shape: valid_len out of int32 range")
+        return np.ascontiguousarray(v.astype(np.int32))
+
+
+def make_desc(shape: AttnShape, params: AttnParams) -> Desc:
+    m = params.mask
+    return Desc(batch=shape.batch, heads=shape.heads, seq=shape.seq, head_dim=shape.head_dim,
+                block=params.block, mask=m.kind,
+                halo=m.param if m.kind == _lib.MASK_BLOCK else 0,
+                window=m.param if m.kind == _lib.MASK_WINDOW else 0,
+                scale=params.scale)
+
+
+def _i32p(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))
+
+
+def _f32p(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+def _host_f32(name: str, a, writable: bool = False) -> np.ndarray:
+    arr = np.asarray(a)
+    if arr.dtype != np.float32:
+        raise TypeError(f"buffer `{name}` must be float32, got {arr.dtype}")
+    if writable:
+        if not arr.flags["C_CONTIGUOUS"] or not arr.flags["WRITEABLE"]:
+            raise TypeError(f"buffer `{name}` must be a writable C-contiguous array")
+        return arr
+    return np.ascontiguousarray(arr)
+
+
+def validate(shape: AttnShape, params: AttnParams, q, k, v, out) -> None:
+    """attention.rs:128-170 over the batch layout; raises KernelError."""
+    valid = params.valid_array(shape.batch)
+    lens = {n: int(np.asarray(b).size) for n, b in (("q", q), ("k", k), ("v", v), ("out", out))}
+    d = make_desc(shape, params)
+    _check(lib.raya_attn_validate(ctypes.byref(d), _i32p(valid), lens["q"], lens["k"], lens["v"],
+                                  lens["out"]), lens)
+
+
+def work(shape: AttnShape, params: AttnParams) -> tuple[int, int]:
+    """Exact (allowed pairs, valid query rows); FLOPs = 4 * head_dim * pairs."""
+    valid = params.valid_array(shape.batch)
+    d = make_desc(shape, params)
+    pairs, rows = ctypes.c_uint64(), ctypes.c_uint64()
+    _check(lib.raya_attn_work(ctypes.byref(d), _i32p(valid), ctypes.byref(pairs), ctypes.byref(rows)))
+    return pairs.value, rows.value
+
+
+def shard(shape: AttnShape, params: AttnParams, world: int, rank: int) -> tuple[int, int]:
+    """[begin, end) of flattened batch*heads slices owned by ``rank``."""
+    valid = params.valid_array(shape.batch)
+    d = make_desc(shape, params)
+    b, e = ctypes.c_int64(), ctypes.c_int64()
+    _check(lib.raya_attn_shard(ctypes.byref(d), _i32p(valid), world, rank, ctypes.byref(b),
+                               ctypes.byref(e)))
+    return b.value, e.value
+
+
+class AttentionKernel(abc.ABC):
+    """attention.rs:108-125: the single entry point for attention."""
+
+    @abc.abstractmethod
+    def name(self) -> str: ...
+
+    @abc.abstractmethod
+    def attend(self, shape: AttnShape, params: AttnParams, q, k, v, out) -> None: ...
+
+
+@dataclass
+class CudaConfig:
+    """Counterpart of TiledConfig (tiled/mod.rs:14-19): which GPU runs it."""
+
+    device: int = 0
+    kernel: int = field(default=_lib.KERNEL_AUTO)
+
+
+class Cuda(AttentionKernel):
+    """The B200 block-local attention kernel behind the reference's trait."""
+
+    def __init__(self, config: CudaConfig | None = None):
+        self.config = config or CudaConfig()
+
+    def name(self) -> str:
+        return "cuda-b200"
+
+    def attend(self, shape: AttnShape, params: AttnParams, q, k, v, out) -> None:
+        """Host buffers in, host buffer out, synchronous (attention.rs:116-124)."""
+        valid = params.valid_array(shape.batch)
+        qh, kh, vh = _host_f32("q", q), _host_f32("k", k), _host_f32("v", v)
+        oh = _host_f32("out", out, writable=True)
+        lens = {"q": qh.size, "k": kh.size, "v": vh.size, "out": oh.size}
+        d = make_desc(shape, params)
+        _check(lib.raya_attn_forward_host(ctypes.byref(d), _f32p(qh), qh.size, _f32p(kh), kh.size,
+                                          _f32p(vh), vh.size, _f32p(oh), oh.size, _i32p(valid),
+                                          self.config.device), lens)
+
+    def attend_device(self, shape: AttnShape, params: AttnParams, q, k, v, out,
+                      valid_len=None, stream=None, kernel: int | None = None) -> None:
+        """Device tensors (torch CUDA tensors or raw pointers) on ``stream``,
+        asynchronous.  ``valid_len`` is a device int32 tensor / pointer, or
+        None to upload ``params.valid_len`` here (a synchronous copy)."""
+        import torch
+
+        def ptr(x):
+            if isinstance(x, torch.Tensor):
+                if not x.is_cuda or x.dtype not in (torch.float32, torch.int32) or not x.is_contiguous():
+                    raise TypeError("device buffers must be contiguous CUDA float32/int32 tensors")
+                return x.data_ptr()
+            return int(x) if x is not None else None
+
+        keep = None
+        if valid_len is None:
+            keep = torch.from_numpy(params.valid_array(shape.batch)).to(
+                q.device if isinstance(q, torch.Tensor) else "cuda")
+            valid_len = keep
+        if stream is None:
+            stream = torch.cuda.current_stream().cuda_stream
+        elif isinstance(stream, torch.cuda.Stream):
+            stream = stream.cuda_stream
+        d = make_desc(shape, params)
+        kid = self.config.kernel if kernel is None else kernel
+        _check(lib.raya_attn_forward_ex(ctypes.byref(d), ptr(q), ptr(k), ptr(v), ptr(out),
+                                        ptr(valid_len), stream, kid))
+        if keep is not None:  # keep the uploaded lengths alive until the kernel has run
+            _sync(stream)
+
+
+def _sync(stream) -> None:
+    _check(lib.raya_attn_sync_status(ctypes.c_void_p(stream)))
+
+
+def sync_status(stream=None) -> None:
+    """Synchronise ``stream`` and raise DeviceTimeout if a device-side wait
+    gave up since the last check."""
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream().cuda_stream
+    elif isinstance(stream, torch.cuda.Stream):
+        stream = stream.cuda_stream
+    _sync(stream)
+
+
+def fill_normal(tensor, seed: int, stream_id: int, first_index: int = 0, stddev: float = 1.0,
+                stream=None) -> None:
+    """Seeded N(0, stddev^2) values into a CUDA float32 tensor (device-side)."""
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream().cuda_stream
+    _check(lib.raya_attn_fill_normal(tensor.data_ptr(), tensor.numel(), seed, stream_id, first_index,
+                                     stddev, stream))
+
+
+def ffma_peak(reps: int = 5) -> float:
+    """Measured FP32 FFMA throughput of the current GPU, TFLOP/s."""
+    out = ctypes.c_double()
+    _check(lib.raya_attn_ffma_peak(reps, ctypes.byref(out)))
+    return out.value

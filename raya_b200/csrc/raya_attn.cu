@@ -1,0 +1,497 @@
+// raya_attn.cu — the C ABI of libraya_attn.so (include/raya_attn.h):
+// argument validation mirroring raya's `validate`, the host-buffer and
+// device-buffer entry points, kernel launch, exact work counts, the
+// batch x heads shard partition, the seeded device generator and the FFMA
+// throughput probe.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/raya_attn.h"
+#include "common.cuh"
+#include "rowwise.cuh"
+#include "tiled64.cuh"
+
+namespace raya {
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxHeadDim = 256;
+constexpr long long kMaxSeq = 1ll << 29;
+constexpr long long kDefaultTimeoutCycles = 1ll << 31;  // ~1 s at B200 clocks
+constexpr int kTiledStages = 1;
+
+// Device status word: bit 0 = a bounded wait gave up.  One per device that
+// loads the library; its device address is looked up once per device.
+__device__ int g_status;
+
+thread_local std::string t_error = "no error";
+
+raya_attn_status fail(raya_attn_status st, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_error = buf;
+  return st;
+}
+
+raya_attn_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(RAYA_ATTN_ERR_CUDA, "cuda: %s: %s", what, cudaGetErrorString(e));
+}
+
+// Per-device state: status-word address, kernel attributes, staging buffers
+// of the host-buffer entry point.
+struct DeviceCtx {
+  std::mutex mu;
+  bool ready = false;
+  int* status = nullptr;
+  int sms = 0;
+  cudaStream_t stream = nullptr;
+  float* buf[4] = {nullptr, nullptr, nullptr, nullptr};  // q, k, v, out
+  size_t cap = 0;                                        // floats per buffer
+  int32_t* dvalid = nullptr;
+  size_t vcap = 0;
+};
+DeviceCtx g_ctx[kMaxDevices];
+
+raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(RAYA_ATTN_ERR_CUDA, "cuda: device %d out of range", dev);
+  DeviceCtx& c = g_ctx[dev];
+  std::lock_guard<std::mutex> lock(c.mu);
+  if (!c.ready) {
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&c.status), g_status);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    e = cudaDeviceGetAttribute(&c.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SMs)");
+    e = cudaFuncSetAttribute(tiled64::kernel<kTiledStages>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(tiled64::smem_bytes<kTiledStages>()));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tiled64 smem)");
+    c.ready = true;
+  }
+  *out = &c;
+  return RAYA_ATTN_OK;
+}
+
+// Shape checks of validate (attention.rs:136-158), in the reference's order,
+// plus this library's own limits.
+raya_attn_status check_shape(const raya_attn_desc* d) {
+  if (!d) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null descriptor");
+  if (d->heads <= 0 || d->head_dim <= 0)
+    return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: heads and head_dim must be at least 1");
+  if (d->head_dim % 8 != 0)
+    return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: head_dim %lld is not a multiple of 8",
+                static_cast<long long>(d->head_dim));
+  if (d->batch <= 0) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: batch must be at least 1");
+  if (d->seq < 0) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: seq %lld is negative",
+                              static_cast<long long>(d->seq));
+  if (d->mask == RAYA_MASK_BLOCK) {
+    if (d->block < 1)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: block %lld (must be at least 1)",
+                  static_cast<long long>(d->block));
+    if (d->halo < 0) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: halo %d is negative", d->halo);
+  } else if (d->mask == RAYA_MASK_WINDOW) {
+    if (d->window < 0)
+      return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: window %lld is negative",
+                  static_cast<long long>(d->window));
+  } else if (d->mask != RAYA_MASK_FULL) {
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: mask kind %d", d->mask);
+  }
+  if (d->head_dim > kMaxHeadDim)
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: head_dim %lld (at most %d)",
+                static_cast<long long>(d->head_dim), kMaxHeadDim);
+  if (d->seq >= kMaxSeq)
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: seq %lld (below %lld)",
+                static_cast<long long>(d->seq), kMaxSeq);
+  if (!std::isfinite(d->scale)) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: scale is not finite");
+  return RAYA_ATTN_OK;
+}
+
+raya_attn_status check_valid(const raya_attn_desc* d, const int32_t* valid_len) {
+  if (!valid_len) return RAYA_ATTN_OK;
+  for (int64_t b = 0; b < d->batch; ++b) {
+    if (valid_len[b] < 0)
+      return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: valid_len %d is negative", valid_len[b]);
+    if (valid_len[b] > d->seq)  // attention.rs:147-152
+      return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: valid_len %d exceeds seq %lld",
+                  valid_len[b], static_cast<long long>(d->seq));
+  }
+  return RAYA_ATTN_OK;
+}
+
+size_t numel(const raya_attn_desc* d) {
+  return static_cast<size_t>(d->batch) * d->heads * d->seq * d->head_dim;
+}
+
+AttnArgs make_args(const raya_attn_desc* d, const float* q, const float* k, const float* v,
+                   float* out, const int32_t* valid_len, int* status) {
+  AttnArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.out = out;
+  a.valid_len = valid_len;
+  a.status = status;
+  a.batch = static_cast<int>(d->batch);
+  a.heads = static_cast<int>(d->heads);
+  a.seq = static_cast<int>(d->seq);
+  a.head_dim = static_cast<int>(d->head_dim);
+  a.mask = d->mask;
+  // Clamp the mask parameters to the sequence (same key ranges, no int32
+  // overflow): a block >= seq puts every row in block 0, a halo past the
+  // block count or a window past seq allows everything.
+  const long long seq = std::max<long long>(d->seq, 1);
+  a.block = static_cast<int>(std::min<long long>(std::max<long long>(d->block, 1), seq));
+  const long long nblocks = (seq + a.block - 1) / a.block;
+  a.halo = static_cast<int>(std::min<long long>(std::max(d->halo, 0), nblocks));
+  a.window = static_cast<int>(std::min<long long>(std::max<long long>(d->window, 0), seq));
+  a.qscale = static_cast<float>(static_cast<double>(d->scale) * 1.4426950408889634);
+  a.row_tiles = static_cast<int>((d->seq + tiled64::kBM - 1) / tiled64::kBM);
+  a.timeout_cycles = kDefaultTimeoutCycles;
+  return a;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launches on the current device, whose context `ctx` is ready.
+raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float* q, const float* k,
+                           const float* v, float* out, const int32_t* valid_len, cudaStream_t stream,
+                           int kernel_id) {
+  if (d->seq == 0) return RAYA_ATTN_OK;  // nothing to write (tiled/mod.rs:79-81)
+  if (!q || !k || !v || !out)
+    return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null tensor pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: tensors must be 16-byte aligned");
+  cudaError_t e;
+  const AttnArgs a = make_args(d, q, k, v, out, valid_len, ctx->status);
+
+  if (kernel_id == RAYA_KERNEL_AUTO) kernel_id = d->head_dim == 64 ? RAYA_KERNEL_TILED64 : RAYA_KERNEL_ROWWISE;
+  if (kernel_id == RAYA_KERNEL_TILED64) {
+    if (d->head_dim != 64)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tiled kernel needs head_dim 64, got %lld",
+                  static_cast<long long>(d->head_dim));
+    const long long grid = static_cast<long long>(d->batch) * d->heads * a.row_tiles;
+    if (grid > 0x7fffffffll)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
+    tiled64::kernel<kTiledStages><<<static_cast<unsigned>(grid), tiled64::kThreads,
+                                    tiled64::smem_bytes<kTiledStages>(), stream>>>(a);
+  } else if (kernel_id == RAYA_KERNEL_ROWWISE) {
+    const long long rows = static_cast<long long>(d->batch) * d->heads * d->seq;
+    const long long want = (rows + rowwise::kWarps - 1) / rowwise::kWarps;
+    const long long grid = std::min<long long>(want, static_cast<long long>(ctx->sms) * 16);
+    rowwise::kernel<<<static_cast<unsigned>(grid), rowwise::kThreads, 0, stream>>>(a);
+  } else {
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: kernel id %d", kernel_id);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+  return RAYA_ATTN_OK;
+}
+
+raya_attn_status launch(const raya_attn_desc* d, const float* q, const float* k, const float* v,
+                        float* out, const int32_t* valid_len, cudaStream_t stream, int kernel_id) {
+  if (d->seq == 0) return RAYA_ATTN_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DeviceCtx* ctx = nullptr;
+  raya_attn_status st = ensure_ready(dev, &ctx);
+  if (st != RAYA_ATTN_OK) return st;
+  return launch_on(ctx, d, q, k, v, out, valid_len, stream, kernel_id);
+}
+
+uint64_t row_pairs(const AttnArgs& a, int valid, int i) {
+  int lo, hi;
+  key_range(a, i, valid, lo, hi);
+  return hi > lo ? static_cast<uint64_t>(hi - lo) : 0;
+}
+
+// Allowed pairs of one (batch entry, head) slice with `valid` valid rows.
+uint64_t slice_pairs(const AttnArgs& a, int valid) {
+  uint64_t p = 0;
+  for (int i = 0; i < valid; ++i) p += row_pairs(a, valid, i);
+  return p;
+}
+
+// splitmix64 (Steele, Lea, Flood 2014) — the generator's mixing function.
+__host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+__global__ void fill_normal_kernel(float* dst, long long n, uint64_t key, long long first,
+                                   float stddev) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long idx = first + i;
+    const uint64_t h = splitmix64(key + static_cast<uint64_t>(idx >> 1));
+    const float u1 = (static_cast<float>(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = (static_cast<float>(h & 0xFFFFFFull) + 0.5f) * (1.0f / 16777216.0f);
+    const float r = sqrtf(-2.0f * logf(u1));
+    float sn, cs;
+    sincospif(2.0f * u2, &sn, &cs);
+    dst[i] = stddev * r * ((idx & 1) ? sn : cs);
+  }
+}
+
+// FFMA throughput probe: 16 independent FMA chains per thread.
+__global__ void __launch_bounds__(256) ffma_probe_kernel(float* sink, int iters, float mul, float add) {
+  float x[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = 1e-3f * threadIdx.x + static_cast<float>(i);
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[i] = fmaf(x[i], mul, add);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) s += x[i];
+  if (s == 1234.5f) sink[blockIdx.x * blockDim.x + threadIdx.x] = s;
+}
+
+}  // namespace
+}  // namespace raya
+
+using namespace raya;
+
+extern "C" {
+
+int raya_attn_version(void) { return RAYA_ATTN_VERSION; }
+
+const char* raya_attn_last_error(void) { return t_error.c_str(); }
+
+raya_attn_status raya_attn_validate(const raya_attn_desc* desc, const int32_t* valid_len,
+                                    size_t q_len, size_t k_len, size_t v_len, size_t out_len) {
+  raya_attn_status st = check_shape(desc);
+  if (st != RAYA_ATTN_OK) return st;
+  st = check_valid(desc, valid_len);
+  if (st != RAYA_ATTN_OK) return st;
+  const size_t expected = numel(desc);
+  const struct { const char* name; size_t got; } bufs[4] = {
+      {"q", q_len}, {"k", k_len}, {"v", v_len}, {"out", out_len}};
+  for (const auto& b : bufs)  // attention.rs:159-168
+    if (b.got != expected)
+      return fail(RAYA_ATTN_ERR_LENGTH, "buffer `%s` has length %zu, expected %zu", b.name, b.got,
+                  expected);
+  return RAYA_ATTN_OK;
+}
+
+raya_attn_status raya_attn_forward_ex(const raya_attn_desc* desc, const float* q, const float* k,
+                                      const float* v, float* out, const int32_t* valid_len,
+                                      void* stream, int kernel_id) {
+  raya_attn_status st = check_shape(desc);
+  if (st != RAYA_ATTN_OK) return st;
+  return launch(desc, q, k, v, out, valid_len, static_cast<cudaStream_t>(stream), kernel_id);
+}
+
+raya_attn_status raya_attn_forward(const raya_attn_desc* desc, const float* q, const float* k,
+                                   const float* v, float* out, const int32_t* valid_len,
+                                   void* stream) {
+  return raya_attn_forward_ex(desc, q, k, v, out, valid_len, stream, RAYA_KERNEL_AUTO);
+}
+
+raya_attn_status raya_attn_sync_status(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  int dev = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DeviceCtx* ctx = nullptr;
+  raya_attn_status st = ensure_ready(dev, &ctx);
+  if (st != RAYA_ATTN_OK) return st;
+  int flag = 0;
+  e = cudaMemcpy(&flag, ctx->status, sizeof flag, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read status");
+  if (flag != 0) {
+    const int zero = 0;
+    e = cudaMemcpy(ctx->status, &zero, sizeof zero, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "clear status");
+    return fail(RAYA_ATTN_ERR_TIMEOUT, "timeout: a device-side wait gave up (status 0x%x)", flag);
+  }
+  return RAYA_ATTN_OK;
+}
+
+raya_attn_status raya_attn_forward_host(const raya_attn_desc* desc, const float* q, size_t q_len,
+                                        const float* k, size_t k_len, const float* v, size_t v_len,
+                                        float* out, size_t out_len, const int32_t* valid_len,
+                                        int device) {
+  raya_attn_status st = raya_attn_validate(desc, valid_len, q_len, k_len, v_len, out_len);
+  if (st != RAYA_ATTN_OK) return st;
+  const size_t n = numel(desc);
+  if (n == 0) return RAYA_ATTN_OK;
+  if (!q || !k || !v || !out) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null buffer");
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  DeviceCtx* ctx = nullptr;
+  st = ensure_ready(device, &ctx);
+  if (st != RAYA_ATTN_OK) return st;
+  std::lock_guard<std::mutex> lock(ctx->mu);  // one host call per device at a time
+  if (!ctx->stream) {
+    e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
+  }
+  if (ctx->cap < n) {
+    for (auto& p : ctx->buf) {
+      if (p) cudaFree(p);
+      p = nullptr;
+    }
+    ctx->cap = 0;
+    for (auto& p : ctx->buf) {
+      e = cudaMalloc(&p, n * sizeof(float));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(staging)");
+    }
+    ctx->cap = n;
+  }
+  if (valid_len && ctx->vcap < static_cast<size_t>(desc->batch)) {
+    if (ctx->dvalid) cudaFree(ctx->dvalid);
+    ctx->dvalid = nullptr;
+    ctx->vcap = 0;
+    e = cudaMalloc(&ctx->dvalid, desc->batch * sizeof(int32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(valid_len)");
+    ctx->vcap = desc->batch;
+  }
+  cudaStream_t s = ctx->stream;
+  const size_t bytes = n * sizeof(float);
+  const float* src[3] = {q, k, v};
+  for (int i = 0; i < 3; ++i) {
+    e = cudaMemcpyAsync(ctx->buf[i], src[i], bytes, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(e, "copy inputs to device");
+  }
+  if (valid_len) {
+    e = cudaMemcpyAsync(ctx->dvalid, valid_len, desc->batch * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(e, "copy valid_len to device");
+  }
+  st = launch_on(ctx, desc, ctx->buf[0], ctx->buf[1], ctx->buf[2], ctx->buf[3],
+                 valid_len ? ctx->dvalid : nullptr, s, RAYA_KERNEL_AUTO);
+  if (st != RAYA_ATTN_OK) return st;
+  e = cudaMemcpyAsync(out, ctx->buf[3], bytes, cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return cuda_fail(e, "copy out to host");
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  int flag = 0;
+  e = cudaMemcpy(&flag, ctx->status, sizeof flag, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read status");
+  if (flag != 0) {
+    const int zero = 0;
+    cudaMemcpy(ctx->status, &zero, sizeof zero, cudaMemcpyHostToDevice);
+    return fail(RAYA_ATTN_ERR_TIMEOUT, "timeout: a device-side wait gave up (status 0x%x)", flag);
+  }
+  return RAYA_ATTN_OK;
+}
+
+raya_attn_status raya_attn_work(const raya_attn_desc* desc, const int32_t* valid_len, uint64_t* pairs,
+                                uint64_t* valid_rows) {
+  raya_attn_status st = check_shape(desc);
+  if (st != RAYA_ATTN_OK) return st;
+  st = check_valid(desc, valid_len);
+  if (st != RAYA_ATTN_OK) return st;
+  const AttnArgs a = make_args(desc, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr);
+  std::vector<uint64_t> memo(static_cast<size_t>(desc->seq) + 1, UINT64_MAX);
+  uint64_t p = 0, r = 0;
+  for (int64_t b = 0; b < desc->batch; ++b) {
+    const int valid = valid_len ? valid_len[b] : static_cast<int>(desc->seq);
+    if (memo[valid] == UINT64_MAX) memo[valid] = slice_pairs(a, valid);
+    p += memo[valid] * static_cast<uint64_t>(desc->heads);
+    r += static_cast<uint64_t>(valid) * desc->heads;
+  }
+  if (pairs) *pairs = p;
+  if (valid_rows) *valid_rows = r;
+  return RAYA_ATTN_OK;
+}
+
+raya_attn_status raya_attn_shard(const raya_attn_desc* desc, const int32_t* valid_len, int world,
+                                 int rank, int64_t* bh_begin, int64_t* bh_end) {
+  raya_attn_status st = check_shape(desc);
+  if (st != RAYA_ATTN_OK) return st;
+  st = check_valid(desc, valid_len);
+  if (st != RAYA_ATTN_OK) return st;
+  if (world < 1 || rank < 0 || rank >= world)
+    return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: rank %d of world %d", rank, world);
+  const AttnArgs a = make_args(desc, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr);
+  const int64_t nbh = desc->batch * desc->heads;
+  // Cost of a slice: its allowed pairs plus one unit per row for the stores.
+  std::vector<double> prefix(static_cast<size_t>(nbh) + 1, 0.0);
+  std::vector<double> memo(static_cast<size_t>(desc->seq) + 1, -1.0);
+  for (int64_t bh = 0; bh < nbh; ++bh) {
+    const int valid = valid_len ? valid_len[bh / desc->heads] : static_cast<int>(desc->seq);
+    if (memo[valid] < 0) memo[valid] = static_cast<double>(slice_pairs(a, valid)) + desc->seq;
+    prefix[bh + 1] = prefix[bh] + memo[valid];
+  }
+  auto cut = [&](int r) -> int64_t {  // first slice whose prefix reaches r/world of the total
+    if (r <= 0) return 0;
+    if (r >= world) return nbh;
+    const double target = prefix[nbh] * r / world;
+    const auto it = std::lower_bound(prefix.begin(), prefix.end(), target);
+    int64_t idx = it - prefix.begin();
+    if (idx > 0 && target - prefix[idx - 1] < prefix[idx] - target) --idx;
+    return std::min<int64_t>(idx, nbh);
+  };
+  *bh_begin = cut(rank);
+  *bh_end = std::max(*bh_begin, cut(rank + 1));
+  return RAYA_ATTN_OK;
+}
+
+raya_attn_status raya_attn_fill_normal(float* dst, int64_t n, uint64_t seed, uint32_t stream_id,
+                                       int64_t first_index, float stddev, void* stream) {
+  if (n <= 0) return RAYA_ATTN_OK;
+  if (!dst) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null destination");
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const uint64_t key = splitmix64(seed * 0x100000001B3ull + stream_id);
+  const long long blocks = std::min<long long>((n + 255) / 256, static_cast<long long>(sms) * 8);
+  fill_normal_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      dst, n, key, first_index, stddev);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fill_normal launch");
+  return RAYA_ATTN_OK;
+}
+
+raya_attn_status raya_attn_ffma_peak(int reps, double* tflops) {
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  const int blocks = sms * 8, threads = 256, iters = 16384;
+  float* sink = nullptr;
+  e = cudaMalloc(&sink, sizeof(float) * blocks * threads);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(sink)");
+  cudaEvent_t t0, t1;
+  cudaEventCreate(&t0);
+  cudaEventCreate(&t1);
+  ffma_probe_kernel<<<blocks, threads>>>(sink, iters, 0.99999f, 1e-6f);  // warm-up
+  double best = 0.0;
+  for (int r = 0; r < std::max(reps, 1); ++r) {
+    cudaEventRecord(t0);
+    ffma_probe_kernel<<<blocks, threads>>>(sink, iters, 0.99999f, 1e-6f);
+    cudaEventRecord(t1);
+    cudaEventSynchronize(t1);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, t0, t1);
+    const double flops = 2.0 * 16 * 8 * static_cast<double>(iters) * blocks * threads;
+    best = std::max(best, flops / (ms * 1e-3) / 1e12);
+  }
+  e = cudaGetLastError();
+  cudaEventDestroy(t0);
+  cudaEventDestroy(t1);
+  cudaFree(sink);
+  if (e != cudaSuccess) return cuda_fail(e, "ffma probe");
+  *tflops = best;
+  return RAYA_ATTN_OK;
+}
+
+}  // extern "C"
