@@ -235,8 +235,14 @@ def run_b200(args) -> None:
     params = rb.AttnParams.new(rb.Mask.block(w.halo), valid, D, block=w.block)
     pairs, rows = rb.work(shape, params)
     n = w.numel
-    q, k, v, out = (torch.empty(n, dtype=torch.float32, device=dev) for _ in range(4))
-    fill_device(w, (q, k, v), bh0=b0 * w.heads)
+    # One (q, k, v, out) set per encoder layer (c4 has 12; the others 1).
+    layers = []
+    for layer in range(w.layers):
+        t = tuple(torch.empty(n, dtype=torch.float32, device=dev) for _ in range(4))
+        fill_device(w, t[:3], layer=layer, bh0=b0 * w.heads)
+        layers.append(t)
+    q, k, v, out = layers[0]
+    pairs, rows = pairs * w.layers, rows * w.layers
     dvalid = torch.from_numpy(valid).to(dev)
     kern = rb.Cuda(rb.CudaConfig(device=local, kernel=args.kernel))
     stream = torch.cuda.current_stream(dev)
@@ -246,7 +252,8 @@ def run_b200(args) -> None:
     ffma_tflops = rb.ffma_peak(5)
 
     def step():
-        kern.attend_device(shape, params, q, k, v, out, valid_len=dvalid, stream=stream)
+        for lq, lk, lv, lo in layers:  # layers back to back on one stream
+            kern.attend_device(shape, params, lq, lk, lv, lo, valid_len=dvalid, stream=stream)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -279,10 +286,11 @@ def run_b200(args) -> None:
     gflops = flops_all / (ms_max * 1e-3) / 1e9
     qps = rows_all / (ms_max * 1e-3)
 
-    # Roofline of the one kernel of a step (per launch on this rank).
-    flops_launch = 4.0 * D * pairs
+    # Roofline of the kernel (per launch on this rank; a step is w.layers launches).
+    flops_launch = 4.0 * D * pairs / w.layers
     bytes_launch = 4.0 * D * (3 * float(valid.sum()) + w.batch * w.seq) * w.heads
-    achieved_tf = flops_launch / (ms * 1e-3) / 1e12
+    launch_ms = ms / w.layers
+    achieved_tf = flops_launch / (launch_ms * 1e-3) / 1e12
     peaks = load_peaks()
     hbm = peaks.get("hbm_gbs")
     tkey = f"{w.name}-halo{w.halo}"
@@ -292,8 +300,8 @@ def run_b200(args) -> None:
                 "nominal_peak": round(148 * 128 * 2 * 1.965e9 / 1e12, 1),
                 "traffic": load_traffic(tkey),
                 "algorithmic_bytes": bytes_launch,
-                "hbm": {"achieved": round(bytes_launch / (ms * 1e-3) / 1e9, 1), "peak": hbm,
-                        "unit": "GB/s", "frac": round(bytes_launch / (ms * 1e-3) / 1e9 / hbm, 4) if hbm else None,
+                "hbm": {"achieved": round(bytes_launch / (launch_ms * 1e-3) / 1e9, 1), "peak": hbm,
+                        "unit": "GB/s", "frac": round(bytes_launch / (launch_ms * 1e-3) / 1e9 / hbm, 4) if hbm else None,
                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if hbm else None}}
 
     # End to end through the host-buffer API (pinned inputs, synchronous).
@@ -314,12 +322,20 @@ def run_b200(args) -> None:
             t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_s = float(t[0])
-        e2e = {"value": round(flops_all / e2e_s / 1e9, 3), "unit": "GFLOP/s",
+        e2e = {"value": round(flops_all / w.layers / e2e_s / 1e9, 3), "unit": "GFLOP/s",
                "ms_per_step": round(e2e_s * 1e3, 3),
                "h2d_bytes_per_step": 3 * n * 4 + w.batch * 4, "d2h_bytes_per_step": n * 4,
                "api": "raya_attn_forward_host (AttentionKernel::attend contract), pinned host buffers"}
         # the host call must agree with the device call bit for bit
         assert torch.equal(ho, out.cpu()), "host-buffer call differs from the device call"
+
+    # Stage proportions of one extra, instrumented launch (the reference
+    # bench's "stages" field, benches/local_attention.rs:127-130,155-157).
+    stages = None
+    if args.kernel != 2:
+        st = rb.stage_times(shape, params, q, k, v, out, valid_len=dvalid,
+                            kernel=args.kernel or rb.KERNEL_TILED64)
+        stages = {key: round(val, 2) for key, val in st.items() if key.endswith("pct")}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -338,9 +354,9 @@ def run_b200(args) -> None:
         "config": workload_config(w, world),
         "queries_per_s": round(qps, 1),
         "frac_fp32_peak": roofline["frac"],
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * w.layers,
         "kernel": "tiled64 (raya_b200/csrc/tiled64.cuh)" if args.kernel in (0, 1) else "rowwise",
-        "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+        "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "stages": stages,
     }
     print(json.dumps(line), flush=True)
 

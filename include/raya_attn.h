@@ -74,8 +74,14 @@ typedef struct {
 /* Kernel selection for raya_attn_forward_ex (tests and benchmarks). */
 typedef enum {
   RAYA_KERNEL_AUTO = 0,     /* tiled FFMA kernel when head_dim == 64, else rowwise */
-  RAYA_KERNEL_TILED64 = 1,  /* 128-row CTA tiles, TMA-staged 64-key tiles, head_dim 64 */
-  RAYA_KERNEL_ROWWISE = 2   /* one warp per query row, any head_dim */
+  RAYA_KERNEL_TILED64 = 1,  /* the tuned tiled variant (TMA-staged 64-key tiles, head_dim 64) */
+  RAYA_KERNEL_ROWWISE = 2,  /* one warp per query row, any head_dim */
+  /* Fixed variants of the tiled kernel (warps of 32 query rows per CTA,
+   * K/V stages), for benchmarks and tests. */
+  RAYA_KERNEL_TILED64_W4S1 = 16,
+  RAYA_KERNEL_TILED64_W2S1 = 17,
+  RAYA_KERNEL_TILED64_W4S2 = 18,
+  RAYA_KERNEL_TILED64_W2S2 = 19
 } raya_kernel_id;
 
 /* Argument checks of validate (attention.rs:128-170), extended to the batch
@@ -115,6 +121,20 @@ raya_attn_status raya_attn_forward_ex(const raya_attn_desc* desc, const float* q
                                       const float* k, const float* v, float* out,
                                       const int32_t* valid_len, void* stream,
                                       int kernel_id);
+
+/* Stage timing, the counterpart of Tiled::attend_with_stages / StageTimes
+ * (tiled/mod.rs:60-126, tiled/stages.rs:1-31): raya_attn_forward_ex with a
+ * tiled kernel (kernel_id AUTO, TILED64 or a TILED64_* variant) whose warps
+ * read clock64 around each stage and add their cycle counts into
+ * stage_cycles, a DEVICE array of 8 uint64 that the caller zeroes:
+ * [0] QK^T, [1] softmax, [2] P.V, [3] K-tile wait, [4] V-tile wait,
+ * [5] next-tile refill, [6] warp-tiles processed, [7] total cycles.  Like the
+ * reference's stage-timing build, the clocks perturb the run slightly: read
+ * the counters as proportions. */
+raya_attn_status raya_attn_forward_timed(const raya_attn_desc* desc, const float* q,
+                                         const float* k, const float* v, float* out,
+                                         const int32_t* valid_len, void* stream,
+                                         int kernel_id, uint64_t* stage_cycles);
 
 /* Synchronises `stream` and returns RAYA_ATTN_ERR_TIMEOUT if any kernel of
  * this library on the current device recorded a bounded-wait timeout since

@@ -15,13 +15,14 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libraya_attn.so")
 OK, ERR_SHAPE, ERR_LENGTH, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_NCCL = range(7)
 MASK_BLOCK, MASK_WINDOW, MASK_FULL = 0, 1, 2
 KERNEL_AUTO, KERNEL_TILED64, KERNEL_ROWWISE = 0, 1, 2
+KERNEL_TILED64_VARIANTS = {"w4s1": 16, "w2s1": 17, "w4s2": 18, "w2s2": 19}
 
 # Every symbol include/raya_attn.h declares (checked by the ABI test).
 EXPORTS = (
     "raya_attn_validate", "raya_attn_forward_host", "raya_attn_forward",
     "raya_attn_forward_ex", "raya_attn_sync_status", "raya_attn_last_error",
     "raya_attn_work", "raya_attn_shard", "raya_attn_fill_normal",
-    "raya_attn_ffma_peak", "raya_attn_version",
+    "raya_attn_ffma_peak", "raya_attn_version", "raya_attn_forward_timed",
 )
 
 
@@ -44,7 +45,7 @@ class Desc(ctypes.Structure):
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"{LIB_PATH} is not built; run `python -m raya_b200.build` (the CUDA path has no fallback)")
+            f"{LIB_PATH} is not built; run `python raya_b200/build.py` (the CUDA path has no fallback)")
     lib = ctypes.CDLL(LIB_PATH)
     fp = ctypes.POINTER(ctypes.c_float)
     ip = ctypes.POINTER(ctypes.c_int32)
@@ -60,6 +61,8 @@ def _load() -> ctypes.CDLL:
     lib.raya_attn_forward.restype = st
     lib.raya_attn_forward_ex.argtypes = [dp, vp, vp, vp, vp, vp, vp, ctypes.c_int]
     lib.raya_attn_forward_ex.restype = st
+    lib.raya_attn_forward_timed.argtypes = [dp, vp, vp, vp, vp, vp, vp, ctypes.c_int, vp]
+    lib.raya_attn_forward_timed.restype = st
     lib.raya_attn_sync_status.argtypes = [vp]
     lib.raya_attn_sync_status.restype = st
     lib.raya_attn_last_error.argtypes = []

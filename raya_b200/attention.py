@@ -303,6 +303,41 @@ class Cuda(AttentionKernel):
             _sync(stream)
 
 
+STAGE_NAMES = ("qk", "softmax", "pv", "k_wait", "v_wait", "refill", "tiles", "total")
+
+
+def stage_times(shape: AttnShape, params: AttnParams, q, k, v, out, valid_len=None,
+                kernel: int = _lib.KERNEL_TILED64, stream=None) -> dict:
+    """Runs the tiled kernel once with per-stage clocks (the counterpart of
+    Tiled::attend_with_stages, tiled/mod.rs:60-126) and returns the summed
+    warp cycles per stage plus qk/softmax/pv percentages of their total
+    (StageTimes::percentages, tiled/stages.rs:19-31)."""
+    import torch
+
+    dev = q.device
+    counters = torch.zeros(len(STAGE_NAMES), dtype=torch.int64, device=dev)
+    keep = valid_len
+    if keep is None:
+        keep = torch.from_numpy(params.valid_array(shape.batch)).to(dev)
+    if stream is None:
+        stream = torch.cuda.current_stream(dev).cuda_stream
+    d = make_desc(shape, params)
+    _check(lib.raya_attn_forward_timed(ctypes.byref(d), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                       out.data_ptr(), keep.data_ptr(), stream, kernel,
+                                       counters.data_ptr()))
+    _sync(stream)
+    c = dict(zip(STAGE_NAMES, (int(x) for x in counters.cpu().tolist())))
+    work_cycles = c["qk"] + c["softmax"] + c["pv"]
+    if work_cycles:
+        c["qk_pct"] = 100.0 * c["qk"] / work_cycles
+        c["softmax_pct"] = 100.0 * c["softmax"] / work_cycles
+        c["pv_pct"] = 100.0 * c["pv"] / work_cycles
+    if c["total"]:
+        for name in ("qk", "softmax", "pv", "k_wait", "v_wait", "refill"):
+            c[name + "_of_total_pct"] = 100.0 * c[name] / c["total"]
+    return c
+
+
 def _sync(stream) -> None:
     _check(lib.raya_attn_sync_status(ctypes.c_void_p(stream)))
 

@@ -1,8 +1,11 @@
 """Builds libraya_attn.so in-tree (raya_b200/_lib/) with nvcc for sm_100a.
 
-    python -m raya_b200.build          # build if sources are newer
-    python -m raya_b200.build --force  # rebuild
-    python -m raya_b200.build --ptxas  # also print -Xptxas -v resource usage
+    python raya_b200/build.py          # build if sources are newer
+    python raya_b200/build.py --force  # rebuild
+    python raya_b200/build.py --ptxas  # also print -Xptxas -v resource usage
+
+It is run as a script (or loaded by file path from __graft_entry__.build()):
+importing the raya_b200 package loads the library, which may not exist yet.
 
 The library is a plain shared object with a C ABI (include/raya_attn.h); the
 CUDA runtime is linked statically, so it loads next to torch's own runtime.

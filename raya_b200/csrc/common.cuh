@@ -31,6 +31,21 @@ struct AttnArgs {
   float qscale;       // softmax scale * log2(e): scores go through ex2
   int row_tiles;      // CTA row tiles per (batch, head) slice
   long long timeout_cycles;  // bound of every spin wait
+  unsigned long long* stage_cycles;  // device [kStageSlots] or nullptr (timed kernels only)
+};
+
+// Stage-timing slots (the counterpart of StageTimes, tiled/stages.rs:1-31):
+// cycles summed over warps, plus warp-tiles processed.
+enum StageSlot : int {
+  kStageQk = 0,      // QK^T register tile (and the per-element mask)
+  kStageSoftmax = 1, // row max, exponentials, rescale, P to shared memory
+  kStagePv = 2,      // P.V register tile
+  kStageKWait = 3,   // waiting for a K tile
+  kStageVWait = 4,   // waiting for a V tile
+  kStageRefill = 5,  // last-warp bookkeeping and TMA issue of the next tile
+  kStageTiles = 6,   // warp-tiles with work
+  kStageTotal = 7,   // cycles from the first wait to the end of the key loop
+  kStageSlots = 8
 };
 
 // Keys [lo, hi) that query row i may attend, clipped to valid: the rule of
@@ -135,6 +150,19 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 __device__ __forceinline__ void st_stream(float* p, float4 v) { __stcs(reinterpret_cast<float4*>(p), v); }
+
+// Explicit shared-space accesses on 32-bit shared addresses (LDS/STS).
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ void sts32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v));
+}
 
 #endif  // __CUDACC__
 

@@ -26,7 +26,25 @@ constexpr int kMaxDevices = 64;
 constexpr int kMaxHeadDim = 256;
 constexpr long long kMaxSeq = 1ll << 29;
 constexpr long long kDefaultTimeoutCycles = 1ll << 31;  // ~1 s at B200 clocks
-constexpr int kTiledStages = 1;
+
+// The tiled kernel's instantiations: (warps per CTA, K/V stages).
+struct TiledVariant {
+  int id;
+  int warps;
+  int stages;
+  void (*fn)(AttnArgs);
+  void (*timed)(AttnArgs);  // the same kernel with per-stage clocks
+  size_t smem;
+};
+template <int W, int S>
+constexpr TiledVariant variant(int id) {
+  return {id, W, S, tiled64::tiled64_fwd<W, S, false>, tiled64::tiled64_fwd<W, S, true>,
+          tiled64::smem_bytes<W, S>()};
+}
+const TiledVariant kTiled[] = {
+    variant<4, 1>(RAYA_KERNEL_TILED64_W4S1), variant<2, 1>(RAYA_KERNEL_TILED64_W2S1),
+    variant<4, 2>(RAYA_KERNEL_TILED64_W4S2), variant<2, 2>(RAYA_KERNEL_TILED64_W2S2)};
+constexpr int kTiledDefault = RAYA_KERNEL_TILED64_W4S1;
 
 // Device status word: bit 0 = a bounded wait gave up.  One per device that
 // loads the library; its device address is looked up once per device.
@@ -72,10 +90,13 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
     e = cudaDeviceGetAttribute(&c.sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SMs)");
-    e = cudaFuncSetAttribute(tiled64::kernel<kTiledStages>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(tiled64::smem_bytes<kTiledStages>()));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tiled64 smem)");
+    for (const TiledVariant& tv : kTiled) {
+      for (auto fn : {tv.fn, tv.timed}) {
+        e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tv.smem));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tiled64 smem)");
+      }
+    }
     c.ready = true;
   }
   *out = &c;
@@ -155,7 +176,7 @@ AttnArgs make_args(const raya_attn_desc* d, const float* q, const float* k, cons
   a.halo = static_cast<int>(std::min<long long>(std::max(d->halo, 0), nblocks));
   a.window = static_cast<int>(std::min<long long>(std::max<long long>(d->window, 0), seq));
   a.qscale = static_cast<float>(static_cast<double>(d->scale) * 1.4426950408889634);
-  a.row_tiles = static_cast<int>((d->seq + tiled64::kBM - 1) / tiled64::kBM);
+  a.row_tiles = 1;
   a.timeout_cycles = kDefaultTimeoutCycles;
   return a;
 }
@@ -165,30 +186,39 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // Launches on the current device, whose context `ctx` is ready.
 raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float* q, const float* k,
                            const float* v, float* out, const int32_t* valid_len, cudaStream_t stream,
-                           int kernel_id) {
+                           int kernel_id, unsigned long long* stage_cycles = nullptr) {
   if (d->seq == 0) return RAYA_ATTN_OK;  // nothing to write (tiled/mod.rs:79-81)
   if (!q || !k || !v || !out)
     return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null tensor pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
     return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: tensors must be 16-byte aligned");
   cudaError_t e;
-  const AttnArgs a = make_args(d, q, k, v, out, valid_len, ctx->status);
+  AttnArgs a = make_args(d, q, k, v, out, valid_len, ctx->status);
+  a.stage_cycles = stage_cycles;
 
   if (kernel_id == RAYA_KERNEL_AUTO) kernel_id = d->head_dim == 64 ? RAYA_KERNEL_TILED64 : RAYA_KERNEL_ROWWISE;
-  if (kernel_id == RAYA_KERNEL_TILED64) {
+  if (kernel_id == RAYA_KERNEL_TILED64) kernel_id = kTiledDefault;
+  const TiledVariant* tv = nullptr;
+  for (const TiledVariant& t : kTiled)
+    if (t.id == kernel_id) tv = &t;
+  if (tv) {
     if (d->head_dim != 64)
       return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tiled kernel needs head_dim 64, got %lld",
                   static_cast<long long>(d->head_dim));
+    const int bm = tv->warps * tiled64::kRowsPerWarp;
+    a.row_tiles = static_cast<int>((d->seq + bm - 1) / bm);
     const long long grid = static_cast<long long>(d->batch) * d->heads * a.row_tiles;
     if (grid > 0x7fffffffll)
       return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
-    tiled64::kernel<kTiledStages><<<static_cast<unsigned>(grid), tiled64::kThreads,
-                                    tiled64::smem_bytes<kTiledStages>(), stream>>>(a);
+    auto fn = stage_cycles ? tv->timed : tv->fn;
+    fn<<<static_cast<unsigned>(grid), tv->warps * 32, tv->smem, stream>>>(a);
+  } else if (stage_cycles) {
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: stage timing needs a tiled kernel");
   } else if (kernel_id == RAYA_KERNEL_ROWWISE) {
     const long long rows = static_cast<long long>(d->batch) * d->heads * d->seq;
     const long long want = (rows + rowwise::kWarps - 1) / rowwise::kWarps;
     const long long grid = std::min<long long>(want, static_cast<long long>(ctx->sms) * 16);
-    rowwise::kernel<<<static_cast<unsigned>(grid), rowwise::kThreads, 0, stream>>>(a);
+    rowwise::rowwise_fwd<<<static_cast<unsigned>(grid), rowwise::kThreads, 0, stream>>>(a);
   } else {
     return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: kernel id %d", kernel_id);
   }
@@ -198,7 +228,8 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
 }
 
 raya_attn_status launch(const raya_attn_desc* d, const float* q, const float* k, const float* v,
-                        float* out, const int32_t* valid_len, cudaStream_t stream, int kernel_id) {
+                        float* out, const int32_t* valid_len, cudaStream_t stream, int kernel_id,
+                        unsigned long long* stage_cycles = nullptr) {
   if (d->seq == 0) return RAYA_ATTN_OK;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -206,7 +237,7 @@ raya_attn_status launch(const raya_attn_desc* d, const float* q, const float* k,
   DeviceCtx* ctx = nullptr;
   raya_attn_status st = ensure_ready(dev, &ctx);
   if (st != RAYA_ATTN_OK) return st;
-  return launch_on(ctx, d, q, k, v, out, valid_len, stream, kernel_id);
+  return launch_on(ctx, d, q, k, v, out, valid_len, stream, kernel_id, stage_cycles);
 }
 
 uint64_t row_pairs(const AttnArgs& a, int valid, int i) {
@@ -301,6 +332,17 @@ raya_attn_status raya_attn_forward(const raya_attn_desc* desc, const float* q, c
                                    const float* v, float* out, const int32_t* valid_len,
                                    void* stream) {
   return raya_attn_forward_ex(desc, q, k, v, out, valid_len, stream, RAYA_KERNEL_AUTO);
+}
+
+raya_attn_status raya_attn_forward_timed(const raya_attn_desc* desc, const float* q, const float* k,
+                                         const float* v, float* out, const int32_t* valid_len,
+                                         void* stream, int kernel_id, uint64_t* stage_cycles) {
+  raya_attn_status st = check_shape(desc);
+  if (st != RAYA_ATTN_OK) return st;
+  if (!stage_cycles) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null stage counter buffer");
+  if (kernel_id == RAYA_KERNEL_AUTO) kernel_id = RAYA_KERNEL_TILED64;
+  return launch(desc, q, k, v, out, valid_len, static_cast<cudaStream_t>(stream), kernel_id,
+                reinterpret_cast<unsigned long long*>(stage_cycles));
 }
 
 raya_attn_status raya_attn_sync_status(void* stream) {

@@ -19,7 +19,7 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxD = 256;
 
-__global__ void __launch_bounds__(kThreads) kernel(const __grid_constant__ AttnArgs a) {
+__global__ void __launch_bounds__(kThreads) rowwise_fwd(const __grid_constant__ AttnArgs a) {
   __shared__ __align__(16) float qs[kWarps][kMaxD];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int d = a.head_dim;

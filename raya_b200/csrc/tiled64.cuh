@@ -36,21 +36,20 @@ namespace raya {
 namespace tiled64 {
 
 constexpr int kD = 64;          // head_dim
-constexpr int kWarps = 4;
 constexpr int kRowsPerWarp = 32;
-constexpr int kBM = kWarps * kRowsPerWarp;  // 128 query rows per CTA
 constexpr int kBN = 64;         // keys per tile
 constexpr int kQS = kD + 4;     // padded row stride (floats) of Q, K, V tiles
 constexpr int kPS = kBN + 8;    // padded row stride of the P buffer
-constexpr int kThreads = kWarps * 32;
 constexpr int kRowBytes = kD * 4;
 
-template <int STAGES>
+// WARPS warps of 32 query rows per CTA (CTA rows = 32 * WARPS); STAGES K/V
+// tile buffers.
+template <int WARPS, int STAGES>
 struct Smem {
-  float q[kBM][kQS];
+  float q[WARPS * kRowsPerWarp][kQS];
   float k[STAGES][kBN][kQS];
   float v[STAGES][kBN][kQS];
-  float p[kWarps][kRowsPerWarp][kPS];
+  float p[WARPS][kRowsPerWarp][kPS];
   uint64_t qbar;
   uint64_t kbar[STAGES];
   uint64_t vbar[STAGES];
@@ -79,8 +78,10 @@ __device__ __forceinline__ void stage_rows(float* dst, const float* src, int nva
     tma_load_1d(dst + r * kQS, src + static_cast<size_t>(r) * kD, kRowBytes, bar);
 }
 
-// Returns true in every lane of the warp that is the last of the CTA's warps
-// to finish with a stage (the 4th increment of its counter for this round).
+// Returns true in every lane of the warp that is the last of the CTA's WARPS
+// warps to finish with a stage (the WARPS-th increment of its counter for
+// this round).
+template <int WARPS>
 __device__ __forceinline__ bool arrive_last(int* counter, int lane) {
   __syncwarp();
   int old = 0;
@@ -90,12 +91,15 @@ __device__ __forceinline__ bool arrive_last(int* counter, int lane) {
     __threadfence_block();
   }
   old = __shfl_sync(0xffffffffu, old, 0);
-  return (old & (kWarps - 1)) == kWarps - 1;
+  return old % WARPS == WARPS - 1;
 }
 
 // S[m][n] = q_row(m) . k_key(n) over the 64 columns, sequential in c.
-__device__ __forceinline__ void qk_tile(float (&s)[8][8], const float* __restrict__ qw,
-                                        const float* __restrict__ kw) {
+// qa: shared address of this lane's first Q row (row stride 4 rows);
+// ka: shared address of its first K row (row stride 8 rows).  The four
+// column components are applied component-major so that consecutive FFMAs
+// hit different accumulators.
+__device__ __forceinline__ void qk_tile(float (&s)[8][8], uint32_t qa, uint32_t ka) {
 #pragma unroll
   for (int m = 0; m < 8; ++m)
 #pragma unroll
@@ -104,55 +108,92 @@ __device__ __forceinline__ void qk_tile(float (&s)[8][8], const float* __restric
   for (int c4 = 0; c4 < kD / 4; ++c4) {
     float4 qv[8];
 #pragma unroll
-    for (int m = 0; m < 8; ++m)
-      qv[m] = *reinterpret_cast<const float4*>(qw + m * 4 * kQS + c4 * 4);
+    for (int m = 0; m < 8; ++m) qv[m] = lds128(qa + (m * 4 * kQS + c4 * 4) * 4);
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
-      const float4 kv = *reinterpret_cast<const float4*>(kw + n * 8 * kQS + c4 * 4);
+      const float4 kv = lds128(ka + (n * 8 * kQS + c4 * 4) * 4);
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        s[m][n] = fmaf(qv[m].x, kv.x, s[m][n]);
-        s[m][n] = fmaf(qv[m].y, kv.y, s[m][n]);
-        s[m][n] = fmaf(qv[m].z, kv.z, s[m][n]);
-        s[m][n] = fmaf(qv[m].w, kv.w, s[m][n]);
-      }
+      for (int m = 0; m < 8; ++m) s[m][n] = fmaf(qv[m].x, kv.x, s[m][n]);
+#pragma unroll
+      for (int m = 0; m < 8; ++m) s[m][n] = fmaf(qv[m].y, kv.y, s[m][n]);
+#pragma unroll
+      for (int m = 0; m < 8; ++m) s[m][n] = fmaf(qv[m].z, kv.z, s[m][n]);
+#pragma unroll
+      for (int m = 0; m < 8; ++m) s[m][n] = fmaf(qv[m].w, kv.w, s[m][n]);
     }
   }
 }
 
 // O[m][0..3] += sum_j P[m][j] V[j][4cg..4cg+3]; O[m][4..7] likewise at +32.
-__device__ __forceinline__ void pv_tile(float (&o)[8][8], const float* __restrict__ pw,
-                                        const float* __restrict__ vw) {
+// pa: shared address of this lane's first P row (row stride 4 rows);
+// va: shared address of V row 0, column 4*cg.
+__device__ __forceinline__ void pv_tile(float (&o)[8][8], uint32_t pa, uint32_t va) {
 #pragma unroll 2
   for (int j4 = 0; j4 < kBN / 4; ++j4) {
     float4 pv[8];
 #pragma unroll
-    for (int m = 0; m < 8; ++m)
-      pv[m] = *reinterpret_cast<const float4*>(pw + m * 4 * kPS + j4 * 4);
+    for (int m = 0; m < 8; ++m) pv[m] = lds128(pa + (m * 4 * kPS + j4 * 4) * 4);
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
-      const float4 va = *reinterpret_cast<const float4*>(vw + (j4 * 4 + jj) * kQS);
-      const float4 vb = *reinterpret_cast<const float4*>(vw + (j4 * 4 + jj) * kQS + 32);
+      const float4 x = lds128(va + ((j4 * 4 + jj) * kQS) * 4);
+      const float4 y = lds128(va + ((j4 * 4 + jj) * kQS + 32) * 4);
 #pragma unroll
       for (int m = 0; m < 8; ++m) {
         const float p = jj == 0 ? pv[m].x : jj == 1 ? pv[m].y : jj == 2 ? pv[m].z : pv[m].w;
-        o[m][0] = fmaf(p, va.x, o[m][0]);
-        o[m][1] = fmaf(p, va.y, o[m][1]);
-        o[m][2] = fmaf(p, va.z, o[m][2]);
-        o[m][3] = fmaf(p, va.w, o[m][3]);
-        o[m][4] = fmaf(p, vb.x, o[m][4]);
-        o[m][5] = fmaf(p, vb.y, o[m][5]);
-        o[m][6] = fmaf(p, vb.z, o[m][6]);
-        o[m][7] = fmaf(p, vb.w, o[m][7]);
+        o[m][0] = fmaf(p, x.x, o[m][0]);
+        o[m][1] = fmaf(p, x.y, o[m][1]);
+        o[m][2] = fmaf(p, x.z, o[m][2]);
+        o[m][3] = fmaf(p, x.w, o[m][3]);
+        o[m][4] = fmaf(p, y.x, o[m][4]);
+        o[m][5] = fmaf(p, y.y, o[m][5]);
+        o[m][6] = fmaf(p, y.z, o[m][6]);
+        o[m][7] = fmaf(p, y.w, o[m][7]);
       }
     }
   }
 }
 
-template <int STAGES>
-__global__ void __launch_bounds__(kThreads, 2) kernel(const __grid_constant__ AttnArgs a) {
+// Per-warp stage clock (lane 0 only); compiles to nothing unless TIMED.
+template <bool TIMED>
+struct StageClock {
+  __device__ __forceinline__ void start() {}
+  __device__ __forceinline__ void lap(int) {}
+  __device__ __forceinline__ void tile() {}
+  __device__ __forceinline__ void flush(unsigned long long*, int) {}
+};
+
+template <>
+struct StageClock<true> {
+  long long last = 0, first = 0;
+  unsigned long long acc[kStageSlots] = {};
+  __device__ __forceinline__ void start() { first = last = clock64(); }
+  __device__ __forceinline__ void lap(int slot) {
+    const long long now = clock64();
+    acc[slot] += static_cast<unsigned long long>(now - last);
+    last = now;
+  }
+  __device__ __forceinline__ void tile() { acc[kStageTiles] += 1; }
+  __device__ __forceinline__ void flush(unsigned long long* out, int lane) {
+    acc[kStageTotal] = static_cast<unsigned long long>(clock64() - first);
+    if (out && lane == 0)
+      for (int i = 0; i < kStageSlots; ++i) atomicAdd(out + i, acc[i]);
+  }
+};
+
+template <int WARPS, int STAGES>
+constexpr int min_blocks() {
+  // CTAs per SM that the shared memory allows (228 KB per SM, 1 KB reserved
+  // per CTA), which also sets the register cap of __launch_bounds__.
+  return (228 * 1024) / (static_cast<int>(sizeof(Smem<WARPS, STAGES>)) + 1024);
+}
+
+template <int WARPS, int STAGES, bool TIMED>
+__global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, STAGES>())
+    tiled64_fwd(const __grid_constant__ AttnArgs a) {
+  constexpr int kBM = WARPS * kRowsPerWarp;
+  constexpr int kThreads = WARPS * 32;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  Smem<STAGES>& sm = *reinterpret_cast<Smem<STAGES>*>(smem_raw);
+  Smem<WARPS, STAGES>& sm = *reinterpret_cast<Smem<WARPS, STAGES>*>(smem_raw);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -236,9 +277,11 @@ __global__ void __launch_bounds__(kThreads, 2) kernel(const __grid_constant__ At
     for (int c = 0; c < 8; ++c) o[m][c] = 0.f;
   }
 
-  const float* qw = &sm.q[warp * kRowsPerWarp + rg][0];
-  float* pw_store = &sm.p[warp][rg][cg];
-  const float* pw = &sm.p[warp][rg][0];
+  const uint32_t qa = smem_addr(&sm.q[warp * kRowsPerWarp + rg][0]);
+  const uint32_t pa_store = smem_addr(&sm.p[warp][rg][cg]);
+  const uint32_t pa = smem_addr(&sm.p[warp][rg][0]);
+  StageClock<TIMED> clk;
+  clk.start();
   bool ok = mbar_wait_bounded(&sm.qbar, 0, abort_flag, a.status, a.timeout_cycles);
 
   for (int t = 0; ok && t < ntiles; ++t) {
@@ -249,9 +292,11 @@ __global__ void __launch_bounds__(kThreads, 2) kernel(const __grid_constant__ At
     const bool whole = lo_l <= kt && hi_f >= kt + kBN;
 
     if (!mbar_wait_bounded(&sm.kbar[s], par, abort_flag, a.status, a.timeout_cycles)) { ok = false; break; }
+    clk.lap(kStageKWait);
     float sc[8][8];
     if (active) {
-      qk_tile(sc, qw, &sm.k[s][cg][0]);
+      clk.tile();
+      qk_tile(sc, qa, smem_addr(&sm.k[s][cg][0]));
       if (!whole) {
         // Per-element mask: key j allowed for row i iff lo(i) <= j < hi(i).
         // Rows past valid_len reuse the last valid row's range (their
@@ -269,13 +314,15 @@ __global__ void __launch_bounds__(kThreads, 2) kernel(const __grid_constant__ At
         }
       }
     }
+    clk.lap(kStageQk);
     // Done reading K stage s: the last warp refills it with tile t+STAGES.
-    if (arrive_last(&sm.kdone[s], lane) && t + STAGES < ntiles) {
+    if (arrive_last<WARPS>(&sm.kdone[s], lane) && t + STAGES < ntiles) {
       const int kn = (t_begin + t + STAGES) * kBN;
       stage_rows(&sm.k[s][0][0], kbase + static_cast<size_t>(kn) * kD, min(kBN, valid - kn), kBN,
                  &sm.kbar[s], lane);
       if (lane == 0) sm.kissued[s] += 1;
     }
+    clk.lap(kStageRefill);
 
     if (active) {
 #pragma unroll
@@ -296,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 2) kernel(const __grid_constant__ At
         for (int n = 0; n < 8; ++n) {
           const float p = ex2(fmaf(sc[m][n], qscale, -mbase));
           rs += p;
-          pw_store[(4 * m) * kPS + 8 * n] = p;
+          sts32(pa_store + ((4 * m) * kPS + 8 * n) * 4, p);
         }
         lrow[m] = fmaf(lrow[m], alpha, rs);
 #pragma unroll
@@ -304,16 +351,21 @@ __global__ void __launch_bounds__(kThreads, 2) kernel(const __grid_constant__ At
       }
     }
     __syncwarp();
+    clk.lap(kStageSoftmax);
 
     if (!mbar_wait_bounded(&sm.vbar[s], par, abort_flag, a.status, a.timeout_cycles)) { ok = false; break; }
-    if (active) pv_tile(o, pw, &sm.v[s][0][4 * cg]);
-    if (arrive_last(&sm.vdone[s], lane) && t + STAGES < ntiles) {
+    clk.lap(kStageVWait);
+    if (active) pv_tile(o, pa, smem_addr(&sm.v[s][0][4 * cg]));
+    clk.lap(kStagePv);
+    if (arrive_last<WARPS>(&sm.vdone[s], lane) && t + STAGES < ntiles) {
       const int kn = (t_begin + t + STAGES) * kBN;
       stage_rows(&sm.v[s][0][0], vbase + static_cast<size_t>(kn) * kD, min(kBN, valid - kn), kBN,
                  &sm.vbar[s], lane);
       if (lane == 0) sm.vissued[s] += 1;
     }
+    clk.lap(kStageRefill);
   }
+  clk.flush(a.stage_cycles, lane);
 
   // Epilogue: reduce the per-lane row sums, normalise, store (+0.0f for
   // padded rows; rows past seq are not ours).
@@ -356,9 +408,9 @@ __global__ void __launch_bounds__(kThreads, 2) kernel(const __grid_constant__ At
   }
 }
 
-template <int STAGES>
+template <int WARPS, int STAGES>
 constexpr size_t smem_bytes() {
-  return sizeof(Smem<STAGES>);
+  return sizeof(Smem<WARPS, STAGES>);
 }
 
 }  // namespace tiled64

@@ -6,12 +6,16 @@ import numpy as np
 import oracle
 import raya_b200 as rb
 
-# Parity bar: max-abs 1e-5 over all elements and
-# max-rel 1e-4 over elements whose reference magnitude is at least 1e-3
-# (relative error is ill-posed next to zero).
+# Parity bar: max-abs 1e-5 over all elements (the reference's own bar,
+# goldens.rs:15, equivalence.rs:26) and max-rel 1e-4 over elements whose
+# reference magnitude is at least 1e-2.  Relative error is ill-posed next to
+# zero: outputs are convex combinations of O(1) values, so fp32 rounding
+# leaves ~1e-7 absolute error everywhere.  The golden's own two tensors
+# (Laya's native reference and its PyTorch kernel) differ by 1.1e-4 relative
+# over |ref| >= 1e-3 but by 1.5e-5 over |ref| >= 1e-2 (92% of elements).
 ATOL = 1e-5
 RTOL = 1e-4
-REL_FLOOR = 1e-3
+REL_FLOOR = 1e-2
 
 
 def mask_of(p: oracle.Problem) -> rb.Mask:

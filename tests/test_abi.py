@@ -1,0 +1,144 @@
+"""The C ABI on a host without a GPU: the library loads, exports every entry
+point include/raya_attn.h declares, and its host-side logic (argument
+validation, work counts, the shard partition) behaves like the reference's
+(crates/raya-kernels/src/attention.rs:128-170, tests/oracle.rs:35-78)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+import oracle
+import raya_b200 as rb
+from raya_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    text = open(os.path.join(ROOT, "include", "raya_attn.h")).read()
+    return sorted(set(re.findall(r"\b(raya_attn_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    declared = header_symbols()
+    assert declared, "no declarations found"
+    assert sorted(_lib.EXPORTS) == declared
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True)
+    exported = set(re.findall(r"\bT (raya_attn_\w+)", out.stdout))
+    missing = [s for s in declared if s not in exported]
+    assert not missing, f"not exported: {missing}"
+    for s in declared:
+        assert hasattr(_lib.lib, s)
+    assert _lib.lib.raya_attn_version() == 1
+
+
+def _shape(heads=1, seq=4, d=8, batch=1):
+    return rb.AttnShape(heads=heads, seq=seq, head_dim=d, batch=batch)
+
+
+def test_bad_arguments_are_errors_not_panics():
+    """tests/oracle.rs:35-78, through the library's validate."""
+    shape = _shape()
+    ok = np.zeros(shape.numel(), dtype=np.float32)
+    p = rb.AttnParams.new(rb.Mask.BLOCK3, 4, 8)
+    with pytest.raises(rb.LengthError) as e:
+        rb.validate(shape, p, np.zeros(3, np.float32), ok, ok, ok)
+    assert e.value.name == "q" and e.value.got == 3 and e.value.expected == 32
+    assert str(e.value) == "buffer `q` has length 3, expected 32"
+    with pytest.raises(rb.LengthError) as e:
+        rb.validate(shape, p, ok, ok, ok, np.zeros(3, np.float32))
+    assert e.value.name == "out"
+    bad = _shape(d=12)
+    buf = np.zeros(bad.numel(), np.float32)
+    with pytest.raises(rb.ShapeError, match="not a multiple of 8"):
+        rb.validate(bad, p, buf, buf, buf, buf)
+    with pytest.raises(rb.ShapeError, match="exceeds seq"):
+        rb.validate(shape, rb.AttnParams.new(rb.Mask.BLOCK3, 5, 8), ok, ok, ok, ok)
+    with pytest.raises(rb.ShapeError, match="at least 1"):
+        z = _shape(heads=0)
+        rb.validate(z, p, ok[:0], ok[:0], ok[:0], ok[:0])
+    # The reference rejects block != 128; this library accepts any block >= 1
+    # and rejects block 0 with the same error kind.
+    with pytest.raises(rb.UnsupportedError):
+        rb.validate(shape, rb.AttnParams(rb.Mask.BLOCK3, 0, 4, p.scale), ok, ok, ok, ok)
+    rb.validate(shape, rb.AttnParams(rb.Mask.BLOCK3, 64, 4, p.scale), ok, ok, ok, ok)
+    with pytest.raises(rb.UnsupportedError, match="head_dim"):
+        big = _shape(d=264)
+        b = np.zeros(big.numel(), np.float32)
+        rb.validate(big, p, b, b, b, b)
+
+
+def test_host_call_validates_before_touching_the_gpu():
+    """The host-buffer entry point raises the reference's errors without a
+    device (validation runs first)."""
+    shape = _shape()
+    ok = np.zeros(shape.numel(), dtype=np.float32)
+    p = rb.AttnParams.new(rb.Mask.BLOCK3, 4, 8)
+    with pytest.raises(rb.LengthError):
+        rb.Cuda().attend(shape, p, ok[:3], ok, ok, ok.copy())
+    with pytest.raises(rb.ShapeError):
+        rb.Cuda().attend(shape, rb.AttnParams.new(rb.Mask.BLOCK3, 9, 8), ok, ok, ok, ok.copy())
+
+
+def test_per_sequence_valid_lengths_are_validated():
+    shape = _shape(batch=3)
+    buf = np.zeros(shape.numel(), np.float32)
+    with pytest.raises(rb.ShapeError, match="exceeds seq"):
+        rb.validate(shape, rb.AttnParams.new(rb.Mask.BLOCK3, [4, 5, 1], 8), buf, buf, buf, buf)
+    with pytest.raises(rb.ShapeError, match="negative"):
+        rb.validate(shape, rb.AttnParams.new(rb.Mask.BLOCK3, [4, -1, 1], 8), buf, buf, buf, buf)
+    with pytest.raises(rb.ShapeError):
+        rb.validate(shape, rb.AttnParams.new(rb.Mask.BLOCK3, [4, 4], 8), buf, buf, buf, buf)
+    rb.validate(shape, rb.AttnParams.new(rb.Mask.BLOCK3, [4, 0, 1], 8), buf, buf, buf, buf)
+
+
+@pytest.mark.parametrize("mask,block", [(rb.Mask.BLOCK3, 128), (rb.Mask.block(0), 64), (rb.Mask.block(2), 7),
+                                        (rb.Mask.WINDOW64, 128), (rb.Mask.sliding(3), 128), (rb.Mask.FULL, 128)])
+def test_work_counts_match_the_oracle(mask, block):
+    shape = _shape(heads=3, seq=333, d=64, batch=4)
+    valid = [333, 200, 1, 0]
+    pairs, rows = rb.work(shape, rb.AttnParams.new(mask, valid, 64, block=block))
+    kind = {rb.Mask.WINDOW64.kind: oracle.MASK_WINDOW, rb.Mask.FULL.kind: oracle.MASK_FULL}.get(mask.kind, oracle.MASK_BLOCK)
+    p = oracle.Problem(4, 3, 333, 64, mask=kind, block=block, halo=mask.param, window=mask.param)
+    assert (pairs, rows) == oracle.count(p, valid)
+
+
+def test_mask_mirror_matches_the_oracle_key_range():
+    for mask, kw in ((rb.Mask.BLOCK3, dict(mask=oracle.MASK_BLOCK, block=128, halo=1)),
+                     (rb.Mask.block(0), dict(mask=oracle.MASK_BLOCK, block=128, halo=0)),
+                     (rb.Mask.WINDOW64, dict(mask=oracle.MASK_WINDOW, window=64)),
+                     (rb.Mask.FULL, dict(mask=oracle.MASK_FULL))):
+        p = oracle.Problem(1, 1, 500, 8, **kw)
+        for valid in (500, 333, 0):
+            for i in range(0, 500, 7):
+                r = mask.key_range(i, valid)
+                assert (r.start, r.stop) == oracle.key_range(p, i, valid)
+    assert rb.Mask.BLOCK3.allows(127, 255) and not rb.Mask.BLOCK3.allows(127, 256)
+    assert rb.Mask.WINDOW64.allows(100, 164) and not rb.Mask.WINDOW64.allows(100, 165)
+    assert rb.Mask.BLOCK3.name() == "block3" and rb.Mask.WINDOW64.name() == "window64"
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_shards_tile_the_batch_and_balance_work(world):
+    shape = _shape(heads=12, seq=1024, d=64, batch=32)
+    valid = list(np.random.default_rng(0).integers(512, 1025, 32))
+    params = rb.AttnParams.new(rb.Mask.BLOCK3, valid, 64, block=64)
+    ranges = [rb.shard(shape, params, world, r) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == 32 * 12
+    for (a0, a1), (b0, b1) in zip(ranges, ranges[1:]):
+        assert a1 == b0 and a0 <= a1
+    # balance: per-slice pair counts
+    per = np.repeat([oracle.count(oracle.Problem(1, 1, 1024, 64, mask=0, block=64, halo=1), [v])[0] for v in valid], 12)
+    loads = [per[a:b].sum() for a, b in ranges]
+    assert max(loads) <= per.sum() / world + per.max()
+
+
+def test_shard_rejects_bad_ranks():
+    shape = _shape(batch=2)
+    params = rb.AttnParams.new(rb.Mask.BLOCK3, 4, 8)
+    for world, rank in ((0, 0), (2, 2), (2, -1)):
+        with pytest.raises(rb.ShapeError):
+            rb.shard(shape, params, world, rank)

@@ -19,6 +19,8 @@ from _util import (assert_close, cuda_device_run, cuda_host_run, load_golden,
 pytestmark = pytest.mark.gpu
 
 KERNELS_D64 = [rb.KERNEL_TILED64, rb.KERNEL_ROWWISE]
+# every compiled variant of the tiled kernel (warps per CTA x K/V stages)
+TILED_VARIANTS = [rb.KERNEL_TILED64] + sorted(rb._lib.KERNEL_TILED64_VARIANTS.values())
 B3 = dict(mask=oracle.MASK_BLOCK, block=128, halo=1)
 W64 = dict(mask=oracle.MASK_WINDOW, window=64)
 
@@ -51,7 +53,7 @@ def test_block_local_golden_host_call(cuda_device):
 
 @pytest.mark.parametrize("mask", [B3, W64], ids=["block3", "window64"])
 @pytest.mark.parametrize("seq", [1, 127, 128, 129, 1000, 2048])
-@pytest.mark.parametrize("kernel", KERNELS_D64)
+@pytest.mark.parametrize("kernel", TILED_VARIANTS + [rb.KERNEL_ROWWISE])
 def test_matches_oracle_at_edge_lengths(cuda_device, mask, seq, kernel):
     """equivalence.rs:29-42."""
     heads = 2 if seq >= 1000 else 3
@@ -158,7 +160,7 @@ def test_nothing_valid_gives_all_zero_rows(cuda_device):
 
 @pytest.mark.parametrize("block", [32, 64, 128, 256, 48, 7, 1])
 @pytest.mark.parametrize("halo", [0, 1, 2])
-@pytest.mark.parametrize("kernel", KERNELS_D64)
+@pytest.mark.parametrize("kernel", TILED_VARIANTS + [rb.KERNEL_ROWWISE])
 def test_block_sizes_halos_and_ragged_batches(cuda_device, block, halo, kernel):
     """Extensions: any block size, halo, batch > 1 with per-sequence valid_len."""
     p = oracle.Problem(3, 2, 700, 64, mask=oracle.MASK_BLOCK, block=block, halo=halo)
@@ -170,7 +172,7 @@ def test_block_sizes_halos_and_ragged_batches(cuda_device, block, halo, kernel):
 
 
 @pytest.mark.parametrize("window", [0, 1, 31, 64, 100, 500])
-@pytest.mark.parametrize("kernel", KERNELS_D64)
+@pytest.mark.parametrize("kernel", TILED_VARIANTS + [rb.KERNEL_ROWWISE])
 def test_windows_and_ragged_batches(cuda_device, window, kernel):
     p = oracle.Problem(2, 2, 520, 64, mask=oracle.MASK_WINDOW, window=window)
     q, k, v = oracle.qkv(p.numel, 2000 + window)
