@@ -355,7 +355,8 @@ def run_b200(args) -> None:
         "queries_per_s": round(qps, 1),
         "frac_fp32_peak": roofline["frac"],
         "gpu_launches": args.steps * w.layers,
-        "kernel": "tiled64 (raya_b200/csrc/tiled64.cuh)" if args.kernel in (0, 1) else "rowwise",
+        "kernel": "rowwise (raya_b200/csrc/rowwise.cuh)" if args.kernel == 2 else
+                  f"tiled64 (raya_b200/csrc/tiled64.cuh), kernel id {args.kernel or 1}",
         "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "stages": stages,
     }
     print(json.dumps(line), flush=True)

@@ -76,12 +76,12 @@ typedef enum {
   RAYA_KERNEL_AUTO = 0,     /* tiled FFMA kernel when head_dim == 64, else rowwise */
   RAYA_KERNEL_TILED64 = 1,  /* the tuned tiled variant (TMA-staged 64-key tiles, head_dim 64) */
   RAYA_KERNEL_ROWWISE = 2,  /* one warp per query row, any head_dim */
-  /* Fixed variants of the tiled kernel (warps of 32 query rows per CTA,
-   * K/V stages), for benchmarks and tests. */
-  RAYA_KERNEL_TILED64_W4S1 = 16,
-  RAYA_KERNEL_TILED64_W2S1 = 17,
-  RAYA_KERNEL_TILED64_W4S2 = 18,
-  RAYA_KERNEL_TILED64_W2S2 = 19
+  /* Fixed variants of the tiled kernel for benchmarks and tests: W = warps
+   * per CTA, R = query rows per warp (CTA rows = W * R). */
+  RAYA_KERNEL_TILED64_W4R32 = 16,
+  RAYA_KERNEL_TILED64_W2R32 = 17,
+  RAYA_KERNEL_TILED64_W8R16 = 18,
+  RAYA_KERNEL_TILED64_W4R16 = 19
 } raya_kernel_id;
 
 /* Argument checks of validate (attention.rs:128-170), extended to the batch

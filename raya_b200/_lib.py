@@ -15,7 +15,7 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libraya_attn.so")
 OK, ERR_SHAPE, ERR_LENGTH, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_NCCL = range(7)
 MASK_BLOCK, MASK_WINDOW, MASK_FULL = 0, 1, 2
 KERNEL_AUTO, KERNEL_TILED64, KERNEL_ROWWISE = 0, 1, 2
-KERNEL_TILED64_VARIANTS = {"w4s1": 16, "w2s1": 17, "w4s2": 18, "w2s2": 19}
+KERNEL_TILED64_VARIANTS = {"w4r32": 16, "w2r32": 17, "w8r16": 18, "w4r16": 19}
 
 # Every symbol include/raya_attn.h declares (checked by the ABI test).
 EXPORTS = (

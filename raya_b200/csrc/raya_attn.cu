@@ -3,6 +3,8 @@
 // device-buffer entry points, kernel launch, exact work counts, the
 // batch x heads shard partition, the seeded device generator and the FFMA
 // throughput probe.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -28,29 +30,36 @@ constexpr long long kMaxSeq = 1ll << 29;
 constexpr long long kDefaultTimeoutCycles = 1ll << 31;  // ~1 s at B200 clocks
 
 // The tiled kernel's instantiations: (warps per CTA, K/V stages).
+using TiledFn = void (*)(AttnArgs, tiled64::TmaMaps);
 struct TiledVariant {
   int id;
   int warps;
+  int rows_per_warp;
   int stages;
-  void (*fn)(AttnArgs);
-  void (*timed)(AttnArgs);  // the same kernel with per-stage clocks
+  TiledFn fn;
+  TiledFn timed;  // the same kernel with per-stage clocks
   size_t smem;
 };
-template <int W, int S>
+template <int W, int R, int S>
 constexpr TiledVariant variant(int id) {
-  return {id, W, S, tiled64::tiled64_fwd<W, S, false>, tiled64::tiled64_fwd<W, S, true>,
-          tiled64::smem_bytes<W, S>()};
+  return {id, W, R, S, tiled64::tiled64_fwd<W, R, S, false>, tiled64::tiled64_fwd<W, R, S, true>,
+          tiled64::smem_bytes<W, R, S>()};
 }
 const TiledVariant kTiled[] = {
-    variant<4, 1>(RAYA_KERNEL_TILED64_W4S1), variant<2, 1>(RAYA_KERNEL_TILED64_W2S1),
-    variant<4, 2>(RAYA_KERNEL_TILED64_W4S2), variant<2, 2>(RAYA_KERNEL_TILED64_W2S2)};
-constexpr int kTiledDefault = RAYA_KERNEL_TILED64_W4S1;
+    variant<4, 32, 1>(RAYA_KERNEL_TILED64_W4R32), variant<2, 32, 1>(RAYA_KERNEL_TILED64_W2R32),
+    variant<8, 16, 1>(RAYA_KERNEL_TILED64_W8R16), variant<4, 16, 1>(RAYA_KERNEL_TILED64_W4R16)};
+constexpr int kTiledDefault = RAYA_KERNEL_TILED64_W4R32;
 
 // Device status word: bit 0 = a bounded wait gave up.  One per device that
 // loads the library; its device address is looked up once per device.
 __device__ int g_status;
 
 thread_local std::string t_error = "no error";
+
+// cuTensorMapEncodeTiled, fetched once from the driver through the runtime
+// (no libcuda link dependency).
+std::once_flag g_encode_once;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 raya_attn_status fail(raya_attn_status st, const char* fmt, ...) {
   char buf[512];
@@ -100,6 +109,29 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
     c.ready = true;
   }
   *out = &c;
+  return RAYA_ATTN_OK;
+}
+
+// A 2-D tensor map over a [rows][64] fp32 tensor with boxes of
+// [box_rows][32 floats], 128-byte swizzle, zero fill out of bounds.
+raya_attn_status encode_rows64(CUtensorMap* map, const float* base, uint64_t rows, uint32_t box_rows) {
+  std::call_once(g_encode_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode) return fail(RAYA_ATTN_ERR_CUDA, "cuda: cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t gdim[2] = {64, rows};
+  const cuuint64_t gstride[1] = {64 * sizeof(float)};
+  const cuuint32_t box[2] = {32, box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim,
+                              gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(RAYA_ATTN_ERR_CUDA, "cuda: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return RAYA_ATTN_OK;
 }
 
@@ -205,13 +237,19 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     if (d->head_dim != 64)
       return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tiled kernel needs head_dim 64, got %lld",
                   static_cast<long long>(d->head_dim));
-    const int bm = tv->warps * tiled64::kRowsPerWarp;
+    const int bm = tv->warps * tv->rows_per_warp;
     a.row_tiles = static_cast<int>((d->seq + bm - 1) / bm);
     const long long grid = static_cast<long long>(d->batch) * d->heads * a.row_tiles;
     if (grid > 0x7fffffffll)
       return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
+    tiled64::TmaMaps maps;
+    const uint64_t rows = static_cast<uint64_t>(d->batch) * d->heads * d->seq;
+    raya_attn_status st = encode_rows64(&maps.q, q, rows, static_cast<uint32_t>(bm));
+    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.k, k, rows, tiled64::kBN);
+    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tiled64::kBN);
+    if (st != RAYA_ATTN_OK) return st;
     auto fn = stage_cycles ? tv->timed : tv->fn;
-    fn<<<static_cast<unsigned>(grid), tv->warps * 32, tv->smem, stream>>>(a);
+    fn<<<static_cast<unsigned>(grid), tv->warps * 32, tv->smem, stream>>>(a, maps);
   } else if (stage_cycles) {
     return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: stage timing needs a tiled kernel");
   } else if (kernel_id == RAYA_KERNEL_ROWWISE) {

@@ -4,31 +4,32 @@
 // runs 8-row micro tiles over 64-key tiles with an online softmax; this is
 // the same algorithm laid out for a B200 SM:
 //
-//   * one CTA per (batch*head slice, 128 query rows); 4 warps of 32 rows;
+//   * one CTA per (batch*head slice, 32*WARPS query rows); 32 rows per warp;
 //   * the CTA's key span (union of its rows' key ranges) is walked in 64-key
-//     tiles.  K and V tiles are staged into shared memory by TMA bulk copies
-//     (one 256-byte row each, into rows padded to 68 floats), and only rows
-//     below valid_len are copied, so padding is never read — as in the
-//     reference, whose key loops stop at valid_len;
+//     tiles.  Q, K and V tiles are staged into shared memory by tensor-map
+//     TMA (cp.async.bulk.tensor.2d, no multicast): each tile is two boxes of
+//     [rows][32 floats] with the 128-byte swizzle, so one tile is two TMA
+//     requests and every LDS.128 below is bank-conflict-free;
 //   * QK^T and PV are FP32 FFMA register tiles: each lane owns 8 rows x 8 keys
 //     of S and 8 rows x 8 columns of O (rows lane/8 + 4m, keys lane%8 + 8n,
-//     columns 4*(lane%8) + {0..3, 32..35}); every LDS.128 feeds 16 FFMAs and
-//     the padded strides make all shared loads conflict-free;
+//     columns 4*(lane%8) + {0..3, 32..35}); every LDS.128 feeds 16 FFMAs;
 //   * online softmax per 64-key tile in registers: row max by three xor
 //     shuffles, p = 2^(s*scale*log2e - m) on the SFU, per-lane partial row
 //     sums (reduced once at the end), O rescaled by alpha;
 //   * P goes through a per-warp shared buffer (stride 72: conflict-free
 //     scalar stores and broadcast LDS.128 loads) into the PV tile;
-//   * K and V are single-buffered per stage; the last warp to finish with a
-//     stage (shared-memory counter) refills it with the next tile, so loads
-//     of K(t+S) overlap softmax/PV(t) and loads of V(t+S) overlap QK(t+S).
-//     Two CTAs fit per SM (106.5 KB shared memory, <= 255 registers).
+//   * K and V have STAGES buffers each; the last warp to finish with a buffer
+//     (an acq_rel shared-memory counter) refills it with the tile STAGES
+//     ahead, so K loads overlap softmax/PV and V loads overlap QK.
 //
-// Semantics kept from the reference: scale applied to q.k (here folded into
-// the exponent), masked keys weigh exactly 0 (ex2(-inf) = +0), padded query
-// rows are written as +0.0f, a row with no allowed key is 0, out is fully
-// overwritten.
+// Padding: a tile may extend past valid_len (or past the slice).  Keys there
+// are masked to -inf before the softmax, and the PV loop stops at valid_len,
+// so no value from a padded K/V row reaches the output — as in the reference,
+// whose key loops stop at valid_len (naive.rs:37, tile.rs:80-87).  Padded
+// query rows are written as +0.0f; a row with no allowed key is 0.
 #pragma once
+
+#include <cuda.h>
 
 #include "common.cuh"
 
@@ -36,20 +37,20 @@ namespace raya {
 namespace tiled64 {
 
 constexpr int kD = 64;          // head_dim
-constexpr int kRowsPerWarp = 32;
 constexpr int kBN = 64;         // keys per tile
-constexpr int kQS = kD + 4;     // padded row stride (floats) of Q, K, V tiles
-constexpr int kPS = kBN + 8;    // padded row stride of the P buffer
-constexpr int kRowBytes = kD * 4;
+constexpr int kHalfCols = 32;   // floats per swizzled box row (128 bytes)
+constexpr int kPS = kBN + 8;    // padded row stride of the P buffer (floats)
 
-// WARPS warps of 32 query rows per CTA (CTA rows = 32 * WARPS); STAGES K/V
-// tile buffers.
-template <int WARPS, int STAGES>
+// Shared-memory layout for WARPS warps of RPW query rows each.  Q, K and V
+// are stored as two column halves of [rows][32 floats], each row 128 bytes
+// with the TMA 128-byte swizzle (16-byte chunk c of row r lives at chunk
+// c ^ (r & 7)); every half starts on a 1024-byte boundary.
+template <int WARPS, int RPW, int STAGES>
 struct Smem {
-  float q[WARPS * kRowsPerWarp][kQS];
-  float k[STAGES][kBN][kQS];
-  float v[STAGES][kBN][kQS];
-  float p[WARPS][kRowsPerWarp][kPS];
+  float q[2][WARPS * RPW][kHalfCols];
+  float k[STAGES][2][kBN][kHalfCols];
+  float v[STAGES][2][kBN][kHalfCols];
+  float p[WARPS][RPW][kPS];
   uint64_t qbar;
   uint64_t kbar[STAGES];
   uint64_t vbar[STAGES];
@@ -60,96 +61,144 @@ struct Smem {
   int abort_flag;
 };
 
-// Warp-collective: zero rows [nvalid, nrows) of a padded tile, then stage
-// rows [0, nvalid) from global memory with one TMA bulk copy per row, all
-// completing on `bar`.  Lane 0 posts the byte count.
-__device__ __forceinline__ void stage_rows(float* dst, const float* src, int nvalid,
-                                           int nrows, uint64_t* bar, int lane) {
-  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int idx = nvalid * 16 + lane; idx < nrows * 16; idx += 32)
-    *reinterpret_cast<float4*>(dst + (idx >> 4) * kQS + (idx & 15) * 4) = zero;
-  __syncwarp();
-  if (lane == 0) {
-    fence_proxy_async_smem();
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nvalid) * kRowBytes);
-  }
-  __syncwarp();
-  for (int r = lane; r < nvalid; r += 32)
-    tma_load_1d(dst + r * kQS, src + static_cast<size_t>(r) * kD, kRowBytes, bar);
+// Tensor maps of the launch: q with boxes of [WARPS*RPW rows][32 floats], k and
+// v with boxes of [64 rows][32 floats]; all over the [batch*heads*seq][64]
+// fp32 view of the tensors, 128-byte swizzle, zero fill out of bounds.
+struct TmaMaps {
+  CUtensorMap q;
+  CUtensorMap k;
+  CUtensorMap v;
+};
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// One thread: post the byte count of a [rows x 64] tile and issue its two
+// column-half boxes.
+__device__ __forceinline__ void stage_tile(float* half0, float* half1, const CUtensorMap* map,
+                                           int y, int rows, uint64_t* bar) {
+  fence_proxy_async_smem();
+  mbar_arrive_expect_tx(bar, static_cast<uint32_t>(rows) * kD * 4);
+  tma_load_2d(half0, map, 0, y, bar);
+  tma_load_2d(half1, map, kHalfCols, y, bar);
+}
+
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "r"(smem_addr(p)), "r"(v)
+               : "memory");
+  return old;
 }
 
 // Returns true in every lane of the warp that is the last of the CTA's WARPS
-// warps to finish with a stage (the WARPS-th increment of its counter for
-// this round).
+// warps to finish with a buffer (the WARPS-th increment of its counter in this
+// round).  __syncwarp orders the warp's shared reads before lane 0's release.
 template <int WARPS>
 __device__ __forceinline__ bool arrive_last(int* counter, int lane) {
   __syncwarp();
   int old = 0;
-  if (lane == 0) {
-    __threadfence_block();
-    old = atomicAdd(counter, 1);
-    __threadfence_block();
-  }
+  if (lane == 0) old = atom_add_acq_rel(counter, 1);
   old = __shfl_sync(0xffffffffu, old, 0);
   return old % WARPS == WARPS - 1;
 }
 
-// S[m][n] = q_row(m) . k_key(n) over the 64 columns, sequential in c.
-// qa: shared address of this lane's first Q row (row stride 4 rows);
-// ka: shared address of its first K row (row stride 8 rows).  The four
-// column components are applied component-major so that consecutive FFMAs
-// hit different accumulators.
-__device__ __forceinline__ void qk_tile(float (&s)[8][8], uint32_t qa, uint32_t ka) {
+// S[m][n] = q_row(m) . k_key(n) over the 64 columns, sequential in c, for
+// the lane's MR rows and 8 keys.  q0: shared address of Q half 0, row
+// (warp rows + rg); rows of m step 4 (512 bytes).  k0: shared address of K
+// half 0, row cg; keys of n step 8 (1024 bytes).  QH: byte size of one Q
+// column half.  Swizzle: row r's chunk c is at c ^ (r & 7); for Q
+// r & 7 = rg + 4*(m & 1) (warp rows start on a multiple of 8), for K r & 7 = cg.
+template <int MR, uint32_t QH>
+__device__ __forceinline__ void qk_tile(float (&s)[MR][8], uint32_t q0, uint32_t k0, int rg, int cg) {
+  constexpr uint32_t KH = kBN * kHalfCols * 4;
 #pragma unroll
-  for (int m = 0; m < 8; ++m)
+  for (int m = 0; m < MR; ++m)
 #pragma unroll
     for (int n = 0; n < 8; ++n) s[m][n] = 0.f;
 #pragma unroll 1
   for (int c4 = 0; c4 < kD / 4; ++c4) {
-    float4 qv[8];
+    const uint32_t half = static_cast<uint32_t>(c4 >> 3);
+    const uint32_t cc = static_cast<uint32_t>(c4 & 7);
+    const uint32_t qe = q0 + half * QH + ((cc ^ static_cast<uint32_t>(rg)) << 4);
+    const uint32_t qo = q0 + half * QH + ((cc ^ static_cast<uint32_t>(rg + 4)) << 4);
+    const uint32_t ka = k0 + half * KH + ((cc ^ static_cast<uint32_t>(cg)) << 4);
+    float4 qv[MR];
 #pragma unroll
-    for (int m = 0; m < 8; ++m) qv[m] = lds128(qa + (m * 4 * kQS + c4 * 4) * 4);
+    for (int m = 0; m < MR; ++m) qv[m] = lds128((m & 1 ? qo : qe) + m * 4 * 128);
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
-      const float4 kv = lds128(ka + (n * 8 * kQS + c4 * 4) * 4);
+      const float4 kv = lds128(ka + n * 8 * 128);
 #pragma unroll
-      for (int m = 0; m < 8; ++m) s[m][n] = fmaf(qv[m].x, kv.x, s[m][n]);
+      for (int m = 0; m < MR; ++m) s[m][n] = fmaf(qv[m].x, kv.x, s[m][n]);
 #pragma unroll
-      for (int m = 0; m < 8; ++m) s[m][n] = fmaf(qv[m].y, kv.y, s[m][n]);
+      for (int m = 0; m < MR; ++m) s[m][n] = fmaf(qv[m].y, kv.y, s[m][n]);
 #pragma unroll
-      for (int m = 0; m < 8; ++m) s[m][n] = fmaf(qv[m].z, kv.z, s[m][n]);
+      for (int m = 0; m < MR; ++m) s[m][n] = fmaf(qv[m].z, kv.z, s[m][n]);
 #pragma unroll
-      for (int m = 0; m < 8; ++m) s[m][n] = fmaf(qv[m].w, kv.w, s[m][n]);
+      for (int m = 0; m < MR; ++m) s[m][n] = fmaf(qv[m].w, kv.w, s[m][n]);
     }
   }
 }
 
-// O[m][0..3] += sum_j P[m][j] V[j][4cg..4cg+3]; O[m][4..7] likewise at +32.
-// pa: shared address of this lane's first P row (row stride 4 rows);
-// va: shared address of V row 0, column 4*cg.
-__device__ __forceinline__ void pv_tile(float (&o)[8][8], uint32_t pa, uint32_t va) {
-#pragma unroll 2
-  for (int j4 = 0; j4 < kBN / 4; ++j4) {
-    float4 pv[8];
+// o[m][:] += p[m] * (V row at shared byte address va: columns 4cg..4cg+3 of
+// half 0 and 32+4cg.. of half 1, already swizzled for that row).
+template <int MR>
+__device__ __forceinline__ void pv_row(float (&o)[MR][8], const float (&p)[MR], uint32_t va) {
+  constexpr uint32_t VH = kBN * kHalfCols * 4;
+  const float4 x = lds128(va);
+  const float4 y = lds128(va + VH);
 #pragma unroll
-    for (int m = 0; m < 8; ++m) pv[m] = lds128(pa + (m * 4 * kPS + j4 * 4) * 4);
+  for (int m = 0; m < MR; ++m) {
+    o[m][0] = fmaf(p[m], x.x, o[m][0]);
+    o[m][1] = fmaf(p[m], x.y, o[m][1]);
+    o[m][2] = fmaf(p[m], x.z, o[m][2]);
+    o[m][3] = fmaf(p[m], x.w, o[m][3]);
+    o[m][4] = fmaf(p[m], y.x, o[m][4]);
+    o[m][5] = fmaf(p[m], y.y, o[m][5]);
+    o[m][6] = fmaf(p[m], y.z, o[m][6]);
+    o[m][7] = fmaf(p[m], y.w, o[m][7]);
+  }
+}
+
+// O[m][:] += sum_{j < nv} P[m][j] V[j][:].  pa: shared address of this lane's
+// first P row (row stride 4 rows); v0: shared address of V half 0 row 0 plus
+// (cg << 4).  Keys go 8 at a time (rows 8*j8 + u hold chunk cg at cg ^ u);
+// keys at or past nv (valid_len inside a partial tile) are never read.
+template <int MR>
+__device__ __forceinline__ void pv_tile(float (&o)[MR][8], uint32_t pa, uint32_t v0, int nv) {
+  const int groups = nv >> 3;
+#pragma unroll 1
+  for (int j8 = 0; j8 < groups; ++j8) {
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const float4 x = lds128(va + ((j4 * 4 + jj) * kQS) * 4);
-      const float4 y = lds128(va + ((j4 * 4 + jj) * kQS + 32) * 4);
+    for (int h = 0; h < 2; ++h) {
+      float4 pv[MR];
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const float p = jj == 0 ? pv[m].x : jj == 1 ? pv[m].y : jj == 2 ? pv[m].z : pv[m].w;
-        o[m][0] = fmaf(p, x.x, o[m][0]);
-        o[m][1] = fmaf(p, x.y, o[m][1]);
-        o[m][2] = fmaf(p, x.z, o[m][2]);
-        o[m][3] = fmaf(p, x.w, o[m][3]);
-        o[m][4] = fmaf(p, y.x, o[m][4]);
-        o[m][5] = fmaf(p, y.y, o[m][5]);
-        o[m][6] = fmaf(p, y.z, o[m][6]);
-        o[m][7] = fmaf(p, y.w, o[m][7]);
+      for (int m = 0; m < MR; ++m) pv[m] = lds128(pa + (m * 4 * kPS + j8 * 8 + h * 4) * 4);
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int u = h * 4 + jj;
+        float p[MR];
+#pragma unroll
+        for (int m = 0; m < MR; ++m)
+          p[m] = jj == 0 ? pv[m].x : jj == 1 ? pv[m].y : jj == 2 ? pv[m].z : pv[m].w;
+        pv_row(o, p, (v0 + (j8 * 8 + u) * 128) ^ static_cast<uint32_t>(u << 4));
       }
     }
+  }
+  // Tail of a partial tile: the last nv % 8 valid keys, one at a time.
+  for (int j = groups * 8; j < nv; ++j) {
+    float p[MR];
+#pragma unroll
+    for (int m = 0; m < MR; ++m) p[m] = lds32(pa + (m * 4 * kPS + j) * 4);
+    pv_row(o, p, (v0 + j * 128) ^ static_cast<uint32_t>((j & 7) << 4));
   }
 }
 
@@ -180,20 +229,32 @@ struct StageClock<true> {
   }
 };
 
-template <int WARPS, int STAGES>
+template <int WARPS, int RPW, int STAGES>
+constexpr size_t smem_bytes() {
+  return sizeof(Smem<WARPS, RPW, STAGES>) + 1024;  // + slack to align the base to 1024 bytes
+}
+
+template <int WARPS, int RPW, int STAGES>
 constexpr int min_blocks() {
   // CTAs per SM that the shared memory allows (228 KB per SM, 1 KB reserved
   // per CTA), which also sets the register cap of __launch_bounds__.
-  return (228 * 1024) / (static_cast<int>(sizeof(Smem<WARPS, STAGES>)) + 1024);
+  return (228 * 1024) / (static_cast<int>(smem_bytes<WARPS, RPW, STAGES>()) + 1024);
 }
 
-template <int WARPS, int STAGES, bool TIMED>
-__global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, STAGES>())
-    tiled64_fwd(const __grid_constant__ AttnArgs a) {
+// WARPS warps of RPW (32 or 16) query rows; each lane owns MR = RPW/4 rows.
+template <int WARPS, int RPW, int STAGES, bool TIMED>
+__global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
+    tiled64_fwd(const __grid_constant__ AttnArgs a, const __grid_constant__ TmaMaps maps) {
+  static_assert(RPW == 16 || RPW == 32, "rows per warp");
+  constexpr int MR = RPW / 4;
+  constexpr int kRowsPerWarp = RPW;
   constexpr int kBM = WARPS * kRowsPerWarp;
   constexpr int kThreads = WARPS * 32;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  Smem<WARPS, STAGES>& sm = *reinterpret_cast<Smem<WARPS, STAGES>*>(smem_raw);
+  constexpr uint32_t kQHalf = kBM * kHalfCols * 4;
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_addr(smem_raw);
+  Smem<WARPS, RPW, STAGES>& sm =
+      *reinterpret_cast<Smem<WARPS, RPW, STAGES>*>(smem_raw + (((raw + 1023u) & ~1023u) - raw));
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -205,8 +266,8 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, STAGES>())
   int valid = a.valid_len ? a.valid_len[b] : seq;
   valid = valid < 0 ? 0 : (valid > seq ? seq : valid);
   const int r0 = tile * kBM;
-  const size_t base = static_cast<size_t>(bh) * seq * kD;
-  float* __restrict__ outp = a.out + base;
+  const long long row_base = bh * seq;  // first row of this slice in the [rows][64] view
+  float* __restrict__ outp = a.out + static_cast<size_t>(row_base) * kD;
 
   if (r0 >= valid) {  // the whole tile is padding: exact zeros, no loads
     const int rows = min(kBM, seq - r0);
@@ -248,36 +309,33 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, STAGES>())
   }
   __syncthreads();
 
-  const float* __restrict__ kbase = a.k + base;
-  const float* __restrict__ vbase = a.v + base;
-  if (warp == 0) {
-    stage_rows(&sm.q[0][0], a.q + base + static_cast<size_t>(r0) * kD, last - r0 + 1,
-               last - r0 + 1, &sm.qbar, lane);
+  if (tid == 0) {
+    stage_tile(&sm.q[0][0][0], &sm.q[1][0][0], &maps.q, static_cast<int>(row_base + r0), kBM, &sm.qbar);
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) {
       if (s < ntiles) {
-        const int kt = (t_begin + s) * kBN;
-        const int nv = min(kBN, valid - kt);
-        stage_rows(&sm.k[s][0][0], kbase + static_cast<size_t>(kt) * kD, nv, kBN, &sm.kbar[s], lane);
-        stage_rows(&sm.v[s][0][0], vbase + static_cast<size_t>(kt) * kD, nv, kBN, &sm.vbar[s], lane);
-        if (lane == 0) { sm.kissued[s] = 1; sm.vissued[s] = 1; }
+        const int y = static_cast<int>(row_base + (t_begin + s) * kBN);
+        stage_tile(&sm.k[s][0][0][0], &sm.k[s][1][0][0], &maps.k, y, kBN, &sm.kbar[s]);
+        stage_tile(&sm.v[s][0][0][0], &sm.v[s][1][0][0], &maps.v, y, kBN, &sm.vbar[s]);
+        sm.kissued[s] = 1;
+        sm.vissued[s] = 1;
       }
     }
   }
 
   volatile int* abort_flag = &sm.abort_flag;
   const float qscale = a.qscale;
-  float o[8][8];
-  float msc[8], lrow[8];
+  float o[MR][8];
+  float msc[MR], lrow[MR];
 #pragma unroll
-  for (int m = 0; m < 8; ++m) {
+  for (int m = 0; m < MR; ++m) {
     msc[m] = -INFINITY;
     lrow[m] = 0.f;
 #pragma unroll
     for (int c = 0; c < 8; ++c) o[m][c] = 0.f;
   }
 
-  const uint32_t qa = smem_addr(&sm.q[warp * kRowsPerWarp + rg][0]);
+  const uint32_t q0 = smem_addr(&sm.q[0][warp * kRowsPerWarp + rg][0]);
   const uint32_t pa_store = smem_addr(&sm.p[warp][rg][cg]);
   const uint32_t pa = smem_addr(&sm.p[warp][rg][0]);
   StageClock<TIMED> clk;
@@ -293,16 +351,17 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, STAGES>())
 
     if (!mbar_wait_bounded(&sm.kbar[s], par, abort_flag, a.status, a.timeout_cycles)) { ok = false; break; }
     clk.lap(kStageKWait);
-    float sc[8][8];
+    float sc[MR][8];
     if (active) {
       clk.tile();
-      qk_tile(sc, qa, smem_addr(&sm.k[s][cg][0]));
+      qk_tile<MR, kQHalf>(sc, q0, smem_addr(&sm.k[s][0][cg][0]), rg, cg);
       if (!whole) {
-        // Per-element mask: key j allowed for row i iff lo(i) <= j < hi(i).
-        // Rows past valid_len reuse the last valid row's range (their
-        // output is overwritten with zeros).
+        // Per-element mask: key j allowed for row i iff lo(i) <= j < hi(i)
+        // (hi <= valid_len, so padded keys are always masked).  Rows past
+        // valid_len reuse the last valid row's range (their output is
+        // overwritten with zeros).
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
+        for (int m = 0; m < MR; ++m) {
           const int i = min(wr0 + rg + 4 * m, wlast);
           int lo, hi;
           key_range(a, i, valid, lo, hi);
@@ -315,18 +374,17 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, STAGES>())
       }
     }
     clk.lap(kStageQk);
-    // Done reading K stage s: the last warp refills it with tile t+STAGES.
-    if (arrive_last<WARPS>(&sm.kdone[s], lane) && t + STAGES < ntiles) {
-      const int kn = (t_begin + t + STAGES) * kBN;
-      stage_rows(&sm.k[s][0][0], kbase + static_cast<size_t>(kn) * kD, min(kBN, valid - kn), kBN,
-                 &sm.kbar[s], lane);
-      if (lane == 0) sm.kissued[s] += 1;
+    // Done reading K buffer s: the last warp refills it with tile t+STAGES.
+    if (arrive_last<WARPS>(&sm.kdone[s], lane) && t + STAGES < ntiles && lane == 0) {
+      const int y = static_cast<int>(row_base + (t_begin + t + STAGES) * kBN);
+      stage_tile(&sm.k[s][0][0][0], &sm.k[s][1][0][0], &maps.k, y, kBN, &sm.kbar[s]);
+      sm.kissued[s] += 1;
     }
     clk.lap(kStageRefill);
 
     if (active) {
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
+      for (int m = 0; m < MR; ++m) {
         float tmax = sc[m][0];
 #pragma unroll
         for (int n = 1; n < 8; ++n) tmax = fmaxf(tmax, sc[m][n]);
@@ -355,13 +413,12 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, STAGES>())
 
     if (!mbar_wait_bounded(&sm.vbar[s], par, abort_flag, a.status, a.timeout_cycles)) { ok = false; break; }
     clk.lap(kStageVWait);
-    if (active) pv_tile(o, pa, smem_addr(&sm.v[s][0][4 * cg]));
+    if (active) pv_tile(o, pa, smem_addr(&sm.v[s][0][0][0]) + (cg << 4), min(kBN, valid - kt));
     clk.lap(kStagePv);
-    if (arrive_last<WARPS>(&sm.vdone[s], lane) && t + STAGES < ntiles) {
-      const int kn = (t_begin + t + STAGES) * kBN;
-      stage_rows(&sm.v[s][0][0], vbase + static_cast<size_t>(kn) * kD, min(kBN, valid - kn), kBN,
-                 &sm.vbar[s], lane);
-      if (lane == 0) sm.vissued[s] += 1;
+    if (arrive_last<WARPS>(&sm.vdone[s], lane) && t + STAGES < ntiles && lane == 0) {
+      const int y = static_cast<int>(row_base + (t_begin + t + STAGES) * kBN);
+      stage_tile(&sm.v[s][0][0][0], &sm.v[s][1][0][0], &maps.v, y, kBN, &sm.vbar[s]);
+      sm.vissued[s] += 1;
     }
     clk.lap(kStageRefill);
   }
@@ -370,7 +427,7 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, STAGES>())
   // Epilogue: reduce the per-lane row sums, normalise, store (+0.0f for
   // padded rows; rows past seq are not ours).
 #pragma unroll
-  for (int m = 0; m < 8; ++m) {
+  for (int m = 0; m < MR; ++m) {
     float l = lrow[m];
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
@@ -406,11 +463,6 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, STAGES>())
       drain(&sm.vbar[s], sm.vissued[s]);
     }
   }
-}
-
-template <int WARPS, int STAGES>
-constexpr size_t smem_bytes() {
-  return sizeof(Smem<WARPS, STAGES>);
 }
 
 }  // namespace tiled64

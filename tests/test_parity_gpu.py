@@ -207,3 +207,26 @@ def test_results_are_bitwise_reproducible_and_shard_invariant(cuda_device):
     a = cuda_device_run(ph, q[:half], k[:half], v[:half], valid=valid[:2])
     b = cuda_device_run(ph, q[half:], k[half:], v[half:], valid=valid[2:])
     assert np.array_equal(np.concatenate([a, b]), one)
+
+
+@pytest.mark.parametrize("mask", [dict(mask=oracle.MASK_BLOCK, block=64, halo=1), W64,
+                                  dict(mask=oracle.MASK_FULL)], ids=["block64", "window64", "full"])
+@pytest.mark.parametrize("kernel", TILED_VARIANTS + [rb.KERNEL_ROWWISE])
+def test_padding_values_never_reach_the_output(cuda_device, mask, kernel):
+    """Rows at or past valid_len are padding: the reference never reads them
+    (naive.rs:37, tile.rs:80-87).  Filled with NaN and Inf here, they must not
+    change a single valid output."""
+    p = oracle.Problem(3, 2, 300, 64, **mask)
+    q, k, v = oracle.qkv(p.numel, 31)
+    valid = [263, 300, 7]
+    q4, k4, v4 = (x.reshape(3, 2, 300, 64) for x in (q, k, v))
+    for b, vl in enumerate(valid):
+        q4[b, :, vl:] = np.nan
+        k4[b, :, vl:] = np.inf
+        v4[b, :, vl:] = np.nan
+    want = oracle.naive(p, q, k, v, valid)
+    assert np.isfinite(want).all()
+    got = cuda_device_run(p, q, k, v, valid=valid, kernel=kernel)
+    assert np.isfinite(got).all()
+    assert_close(got, want, "NaN/Inf padding")
+    padded_rows_exact_zero(got, p, valid)
