@@ -326,8 +326,11 @@ def run_b200(args) -> None:
                "ms_per_step": round(e2e_s * 1e3, 3),
                "h2d_bytes_per_step": 3 * n * 4 + w.batch * 4, "d2h_bytes_per_step": n * 4,
                "api": "raya_attn_forward_host (AttentionKernel::attend contract), pinned host buffers"}
-        # the host call must agree with the device call bit for bit
-        assert torch.equal(ho, out.cpu()), "host-buffer call differs from the device call"
+        # the host call must agree with the device call (bit for bit when both
+        # run the same kernel; --kernel may pick another variant for the device)
+        diff = float((ho - out.cpu()).abs().max())
+        assert diff < 1e-5 and (args.kernel not in (0, 1) or diff == 0.0), \
+            f"host-buffer call differs from the device call by {diff}"
 
     # Stage proportions of one extra, instrumented launch (the reference
     # bench's "stages" field, benches/local_attention.rs:127-130,155-157).

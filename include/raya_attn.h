@@ -73,15 +73,18 @@ typedef struct {
 
 /* Kernel selection for raya_attn_forward_ex (tests and benchmarks). */
 typedef enum {
-  RAYA_KERNEL_AUTO = 0,     /* tiled FFMA kernel when head_dim == 64, else rowwise */
-  RAYA_KERNEL_TILED64 = 1,  /* the tuned tiled variant (TMA-staged 64-key tiles, head_dim 64) */
+  RAYA_KERNEL_AUTO = 0,     /* tiled kernel when head_dim == 64, else rowwise */
+  RAYA_KERNEL_TILED64 = 1,  /* the tuned tiled variant for the mask and block (head_dim 64):
+                               W4R16_P2 for block <= 64 and windows, W4R32_P2 for
+                               block >= 128 and Full */
   RAYA_KERNEL_ROWWISE = 2,  /* one warp per query row, any head_dim */
-  /* Fixed variants of the tiled kernel for benchmarks and tests: W = warps
-   * per CTA, R = query rows per warp (CTA rows = W * R). */
+  /* Fixed variants of the tiled kernel for benchmarks and tests: 4 warps per
+   * CTA of R = 32 or 16 query rows each; P2 = packed FFMA2 (two fused
+   * multiply-adds per instruction) in QK^T and PV (R16) or PV only (R32). */
   RAYA_KERNEL_TILED64_W4R32 = 16,
-  RAYA_KERNEL_TILED64_W2R32 = 17,
-  RAYA_KERNEL_TILED64_W8R16 = 18,
-  RAYA_KERNEL_TILED64_W4R16 = 19
+  RAYA_KERNEL_TILED64_W4R16 = 19,
+  RAYA_KERNEL_TILED64_W4R16_P2 = 20,
+  RAYA_KERNEL_TILED64_W4R32_P2 = 21
 } raya_kernel_id;
 
 /* Argument checks of validate (attention.rs:128-170), extended to the batch
@@ -141,6 +144,14 @@ raya_attn_status raya_attn_forward_timed(const raya_attn_desc* desc, const float
  * the last call (the record is then cleared), RAYA_ATTN_ERR_CUDA on a CUDA
  * error, else OK. */
 raya_attn_status raya_attn_sync_status(void* stream);
+
+/* Failure-detection probe (no reference counterpart): launches one warp that
+ * waits on an mbarrier nothing arrives on, through the same bounded wait as
+ * the attention kernels, limited to `timeout_cycles` (<= 2^31).  The wait
+ * gives up and the kernel returns; the call then reports the recorded
+ * timeout exactly as raya_attn_sync_status does (RAYA_ATTN_ERR_TIMEOUT, the
+ * record cleared).  No GPU fault, trap or hang is involved. */
+raya_attn_status raya_attn_probe_timeout(int64_t timeout_cycles, void* stream);
 
 /* Message of the last error raised on the calling thread (KernelError's
  * Display text for the reference's errors).  Never NULL. */

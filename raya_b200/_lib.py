@@ -15,7 +15,7 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libraya_attn.so")
 OK, ERR_SHAPE, ERR_LENGTH, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_NCCL = range(7)
 MASK_BLOCK, MASK_WINDOW, MASK_FULL = 0, 1, 2
 KERNEL_AUTO, KERNEL_TILED64, KERNEL_ROWWISE = 0, 1, 2
-KERNEL_TILED64_VARIANTS = {"w4r32": 16, "w2r32": 17, "w8r16": 18, "w4r16": 19}
+KERNEL_TILED64_VARIANTS = {"w4r32": 16, "w4r16": 19, "w4r16p2": 20, "w4r32p2": 21}
 
 # Every symbol include/raya_attn.h declares (checked by the ABI test).
 EXPORTS = (
@@ -23,6 +23,7 @@ EXPORTS = (
     "raya_attn_forward_ex", "raya_attn_sync_status", "raya_attn_last_error",
     "raya_attn_work", "raya_attn_shard", "raya_attn_fill_normal",
     "raya_attn_ffma_peak", "raya_attn_version", "raya_attn_forward_timed",
+    "raya_attn_probe_timeout",
 )
 
 
@@ -63,6 +64,8 @@ def _load() -> ctypes.CDLL:
     lib.raya_attn_forward_ex.restype = st
     lib.raya_attn_forward_timed.argtypes = [dp, vp, vp, vp, vp, vp, vp, ctypes.c_int, vp]
     lib.raya_attn_forward_timed.restype = st
+    lib.raya_attn_probe_timeout.argtypes = [ctypes.c_int64, vp]
+    lib.raya_attn_probe_timeout.restype = st
     lib.raya_attn_sync_status.argtypes = [vp]
     lib.raya_attn_sync_status.restype = st
     lib.raya_attn_last_error.argtypes = []

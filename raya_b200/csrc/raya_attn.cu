@@ -28,6 +28,11 @@ constexpr int kMaxDevices = 64;
 constexpr int kMaxHeadDim = 256;
 constexpr long long kMaxSeq = 1ll << 29;
 constexpr long long kDefaultTimeoutCycles = 1ll << 31;  // ~1 s at B200 clocks
+// Host-buffer call: chunks of at least kHostChunkBytes (inputs + output),
+// at most kMaxHostChunks, round-robin over kHostStreams streams.
+constexpr int kHostStreams = 3;
+constexpr int64_t kMaxHostChunks = 16;
+constexpr int64_t kHostChunkBytes = 16ll << 20;
 
 // The tiled kernel's instantiations: (warps per CTA, K/V stages).
 using TiledFn = void (*)(AttnArgs, tiled64::TmaMaps);
@@ -40,15 +45,24 @@ struct TiledVariant {
   TiledFn timed;  // the same kernel with per-stage clocks
   size_t smem;
 };
-template <int W, int R, int S>
+template <int W, int R, int S, bool PQK, bool PPV>
 constexpr TiledVariant variant(int id) {
-  return {id, W, R, S, tiled64::tiled64_fwd<W, R, S, false>, tiled64::tiled64_fwd<W, R, S, true>,
-          tiled64::smem_bytes<W, R, S>()};
+  return {id, W, R, S, tiled64::tiled64_fwd<W, R, S, PQK, PPV, false>,
+          tiled64::tiled64_fwd<W, R, S, PQK, PPV, true>, tiled64::smem_bytes<W, R, S>()};
 }
 const TiledVariant kTiled[] = {
-    variant<4, 32, 1>(RAYA_KERNEL_TILED64_W4R32), variant<2, 32, 1>(RAYA_KERNEL_TILED64_W2R32),
-    variant<8, 16, 1>(RAYA_KERNEL_TILED64_W8R16), variant<4, 16, 1>(RAYA_KERNEL_TILED64_W4R16)};
-constexpr int kTiledDefault = RAYA_KERNEL_TILED64_W4R32;
+    variant<4, 32, 1, false, false>(RAYA_KERNEL_TILED64_W4R32),
+    variant<4, 16, 1, false, false>(RAYA_KERNEL_TILED64_W4R16),
+    variant<4, 16, 1, true, true>(RAYA_KERNEL_TILED64_W4R16_P2),
+    variant<4, 32, 1, false, true>(RAYA_KERNEL_TILED64_W4R32_P2)};
+
+// The tuned choice (measured on B200, profiles/): 64-row CTAs of 16-row warps
+// with packed QK^T and PV for short key spans (block <= 64, windows), 128-row
+// CTAs of 32-row warps with packed PV for long ones (block >= 128, Full).
+int tuned_tiled(const raya_attn_desc* d) {
+  const bool long_span = d->mask == RAYA_MASK_FULL || (d->mask == RAYA_MASK_BLOCK && d->block >= 128);
+  return long_span ? RAYA_KERNEL_TILED64_W4R32_P2 : RAYA_KERNEL_TILED64_W4R16_P2;
+}
 
 // Device status word: bit 0 = a bounded wait gave up.  One per device that
 // loads the library; its device address is looked up once per device.
@@ -82,11 +96,13 @@ struct DeviceCtx {
   bool ready = false;
   int* status = nullptr;
   int sms = 0;
-  cudaStream_t stream = nullptr;
+  cudaStream_t streams[3] = {nullptr, nullptr, nullptr};  // host-buffer call pipeline
+  cudaEvent_t valid_ready = nullptr;
   float* buf[4] = {nullptr, nullptr, nullptr, nullptr};  // q, k, v, out
   size_t cap = 0;                                        // floats per buffer
-  int32_t* dvalid = nullptr;
+  int32_t* dvalid = nullptr;                             // valid length per slice
   size_t vcap = 0;
+  std::vector<int32_t> slice_valid;
 };
 DeviceCtx g_ctx[kMaxDevices];
 
@@ -229,7 +245,7 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
   a.stage_cycles = stage_cycles;
 
   if (kernel_id == RAYA_KERNEL_AUTO) kernel_id = d->head_dim == 64 ? RAYA_KERNEL_TILED64 : RAYA_KERNEL_ROWWISE;
-  if (kernel_id == RAYA_KERNEL_TILED64) kernel_id = kTiledDefault;
+  if (kernel_id == RAYA_KERNEL_TILED64) kernel_id = tuned_tiled(d);
   const TiledVariant* tv = nullptr;
   for (const TiledVariant& t : kTiled)
     if (t.id == kernel_id) tv = &t;
@@ -331,6 +347,22 @@ __global__ void __launch_bounds__(256) ffma_probe_kernel(float* sink, int iters,
   if (s == 1234.5f) sink[blockIdx.x * blockDim.x + threadIdx.x] = s;
 }
 
+// Failure-detection probe: one warp waits on an mbarrier that nothing ever
+// arrives on, through the same bounded wait the attention kernels use, with a
+// short limit.  The wait gives up, records bit 0 of the status word and the
+// kernel returns; the context stays usable.
+__global__ void timeout_probe_kernel(int* status, long long timeout_cycles) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  mbar_wait_bounded(&bar, 0, &abort_flag, status, timeout_cycles);
+}
+
 }  // namespace
 }  // namespace raya
 
@@ -383,6 +415,21 @@ raya_attn_status raya_attn_forward_timed(const raya_attn_desc* desc, const float
                 reinterpret_cast<unsigned long long*>(stage_cycles));
 }
 
+raya_attn_status raya_attn_probe_timeout(int64_t timeout_cycles, void* stream) {
+  if (timeout_cycles < 0 || timeout_cycles > kDefaultTimeoutCycles)
+    return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: timeout of %lld cycles", static_cast<long long>(timeout_cycles));
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DeviceCtx* ctx = nullptr;
+  raya_attn_status st = ensure_ready(dev, &ctx);
+  if (st != RAYA_ATTN_OK) return st;
+  timeout_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(ctx->status, timeout_cycles);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "timeout probe launch");
+  return raya_attn_sync_status(stream);
+}
+
 raya_attn_status raya_attn_sync_status(void* stream) {
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
@@ -419,9 +466,13 @@ raya_attn_status raya_attn_forward_host(const raya_attn_desc* desc, const float*
   st = ensure_ready(device, &ctx);
   if (st != RAYA_ATTN_OK) return st;
   std::lock_guard<std::mutex> lock(ctx->mu);  // one host call per device at a time
-  if (!ctx->stream) {
-    e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
+  if (!ctx->streams[0]) {
+    for (auto& sm : ctx->streams) {
+      e = cudaStreamCreateWithFlags(&sm, cudaStreamNonBlocking);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
+    }
+    e = cudaEventCreateWithFlags(&ctx->valid_ready, cudaEventDisableTiming);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
   }
   if (ctx->cap < n) {
     for (auto& p : ctx->buf) {
@@ -435,32 +486,58 @@ raya_attn_status raya_attn_forward_host(const raya_attn_desc* desc, const float*
     }
     ctx->cap = n;
   }
-  if (valid_len && ctx->vcap < static_cast<size_t>(desc->batch)) {
+  // One valid length per (batch, head) slice, so that any range of slices is
+  // an independent call (batch = #slices, heads = 1).
+  const int64_t nbh = desc->batch * desc->heads;
+  if (ctx->vcap < static_cast<size_t>(nbh)) {
     if (ctx->dvalid) cudaFree(ctx->dvalid);
     ctx->dvalid = nullptr;
     ctx->vcap = 0;
-    e = cudaMalloc(&ctx->dvalid, desc->batch * sizeof(int32_t));
+    e = cudaMalloc(&ctx->dvalid, nbh * sizeof(int32_t));
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(valid_len)");
-    ctx->vcap = desc->batch;
+    ctx->vcap = nbh;
   }
-  cudaStream_t s = ctx->stream;
-  const size_t bytes = n * sizeof(float);
+  ctx->slice_valid.resize(nbh);
+  for (int64_t bh = 0; bh < nbh; ++bh)
+    ctx->slice_valid[bh] = valid_len ? valid_len[bh / desc->heads] : static_cast<int32_t>(desc->seq);
+  e = cudaMemcpyAsync(ctx->dvalid, ctx->slice_valid.data(), nbh * sizeof(int32_t), cudaMemcpyHostToDevice,
+                      ctx->streams[0]);
+  if (e != cudaSuccess) return cuda_fail(e, "copy valid_len to device");
+  e = cudaEventRecord(ctx->valid_ready, ctx->streams[0]);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+
+  // Pipeline over chunks of slices on kHostStreams streams: the copy engines
+  // move chunk c+1 in and chunk c-1 out while chunk c computes.
+  const size_t slice = static_cast<size_t>(desc->seq) * desc->head_dim;
+  const size_t bytes_total = 4 * n * sizeof(float);
+  const int64_t nchunks = std::max<int64_t>(
+      1, std::min<int64_t>({nbh, kMaxHostChunks, static_cast<int64_t>(bytes_total / kHostChunkBytes)}));
   const float* src[3] = {q, k, v};
-  for (int i = 0; i < 3; ++i) {
-    e = cudaMemcpyAsync(ctx->buf[i], src[i], bytes, cudaMemcpyHostToDevice, s);
-    if (e != cudaSuccess) return cuda_fail(e, "copy inputs to device");
+  for (int64_t c = 0; c < nchunks; ++c) {
+    const int64_t bh0 = nbh * c / nchunks, bh1 = nbh * (c + 1) / nchunks;
+    if (bh1 <= bh0) continue;
+    cudaStream_t s = ctx->streams[c % kHostStreams];
+    const size_t off = static_cast<size_t>(bh0) * slice;
+    const size_t cnt = static_cast<size_t>(bh1 - bh0) * slice;
+    for (int i = 0; i < 3; ++i) {
+      e = cudaMemcpyAsync(ctx->buf[i] + off, src[i] + off, cnt * sizeof(float), cudaMemcpyHostToDevice, s);
+      if (e != cudaSuccess) return cuda_fail(e, "copy inputs to device");
+    }
+    e = cudaStreamWaitEvent(s, ctx->valid_ready, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
+    raya_attn_desc sub = *desc;
+    sub.batch = bh1 - bh0;
+    sub.heads = 1;
+    st = launch_on(ctx, &sub, ctx->buf[0] + off, ctx->buf[1] + off, ctx->buf[2] + off, ctx->buf[3] + off,
+                   ctx->dvalid + bh0, s, RAYA_KERNEL_AUTO);
+    if (st != RAYA_ATTN_OK) return st;
+    e = cudaMemcpyAsync(out + off, ctx->buf[3] + off, cnt * sizeof(float), cudaMemcpyDeviceToHost, s);
+    if (e != cudaSuccess) return cuda_fail(e, "copy out to host");
   }
-  if (valid_len) {
-    e = cudaMemcpyAsync(ctx->dvalid, valid_len, desc->batch * sizeof(int32_t), cudaMemcpyHostToDevice, s);
-    if (e != cudaSuccess) return cuda_fail(e, "copy valid_len to device");
+  for (auto& sm : ctx->streams) {
+    e = cudaStreamSynchronize(sm);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
   }
-  st = launch_on(ctx, desc, ctx->buf[0], ctx->buf[1], ctx->buf[2], ctx->buf[3],
-                 valid_len ? ctx->dvalid : nullptr, s, RAYA_KERNEL_AUTO);
-  if (st != RAYA_ATTN_OK) return st;
-  e = cudaMemcpyAsync(out, ctx->buf[3], bytes, cudaMemcpyDeviceToHost, s);
-  if (e != cudaSuccess) return cuda_fail(e, "copy out to host");
-  e = cudaStreamSynchronize(s);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
   int flag = 0;
   e = cudaMemcpy(&flag, ctx->status, sizeof flag, cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "read status");

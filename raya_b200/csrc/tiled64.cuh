@@ -110,19 +110,32 @@ __device__ __forceinline__ bool arrive_last(int* counter, int lane) {
   return old % WARPS == WARPS - 1;
 }
 
-// S[m][n] = q_row(m) . k_key(n) over the 64 columns, sequential in c, for
-// the lane's MR rows and 8 keys.  q0: shared address of Q half 0, row
-// (warp rows + rg); rows of m step 4 (512 bytes).  k0: shared address of K
-// half 0, row cg; keys of n step 8 (1024 bytes).  QH: byte size of one Q
-// column half.  Swizzle: row r's chunk c is at c ^ (r & 7); for Q
-// r & 7 = rg + 4*(m & 1) (warp rows start on a multiple of 8), for K r & 7 = cg.
-template <int MR, uint32_t QH>
+// S[m][n] = q_row(m) . k_key(n) over the 64 columns for the lane's MR rows
+// and 8 keys.  q0: shared address of Q half 0, row (warp rows + rg); rows of
+// m step 4 (512 bytes).  k0: shared address of K half 0, row cg; keys of n
+// step 8 (1024 bytes).  QH: byte size of one Q column half.  Swizzle: row
+// r's chunk c is at c ^ (r & 7); for Q r & 7 = rg + 4*(m & 1) (warp rows
+// start on a multiple of 8), for K r & 7 = cg.
+//
+// P2 = false: one FFMA per product, sequential in c.
+// P2 = true: packed FFMA2 (two FMAs per instruction): even and odd columns
+// accumulate in the two halves of a float2 (both operands are the aligned
+// register pairs of the float4 loads), summed once at the end.
+template <int MR, uint32_t QH, bool P2>
 __device__ __forceinline__ void qk_tile(float (&s)[MR][8], uint32_t q0, uint32_t k0, int rg, int cg) {
   constexpr uint32_t KH = kBN * kHalfCols * 4;
+  float2 acc[MR][P2 ? 8 : 1];
+  if constexpr (P2) {
 #pragma unroll
-  for (int m = 0; m < MR; ++m)
+    for (int m = 0; m < MR; ++m)
 #pragma unroll
-    for (int n = 0; n < 8; ++n) s[m][n] = 0.f;
+      for (int n = 0; n < 8; ++n) acc[m][n] = make_float2(0.f, 0.f);
+  } else {
+#pragma unroll
+    for (int m = 0; m < MR; ++m)
+#pragma unroll
+      for (int n = 0; n < 8; ++n) s[m][n] = 0.f;
+  }
 #pragma unroll 1
   for (int c4 = 0; c4 < kD / 4; ++c4) {
     const uint32_t half = static_cast<uint32_t>(c4 >> 3);
@@ -133,38 +146,71 @@ __device__ __forceinline__ void qk_tile(float (&s)[MR][8], uint32_t q0, uint32_t
     float4 qv[MR];
 #pragma unroll
     for (int m = 0; m < MR; ++m) qv[m] = lds128((m & 1 ? qo : qe) + m * 4 * 128);
+    if constexpr (P2) {
+      // Two keys at a time, so that the two FFMA2s into one accumulator are
+      // 2*MR instructions apart.
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      const float4 kv = lds128(ka + n * 8 * 128);
+      for (int n = 0; n < 8; n += 2) {
+        const float4 k0v = lds128(ka + n * 8 * 128);
+        const float4 k1v = lds128(ka + (n + 1) * 8 * 128);
 #pragma unroll
-      for (int m = 0; m < MR; ++m) s[m][n] = fmaf(qv[m].x, kv.x, s[m][n]);
+        for (int m = 0; m < MR; ++m)
+          acc[m][n] = __ffma2_rn(make_float2(qv[m].x, qv[m].y), make_float2(k0v.x, k0v.y), acc[m][n]);
 #pragma unroll
-      for (int m = 0; m < MR; ++m) s[m][n] = fmaf(qv[m].y, kv.y, s[m][n]);
+        for (int m = 0; m < MR; ++m)
+          acc[m][n + 1] = __ffma2_rn(make_float2(qv[m].x, qv[m].y), make_float2(k1v.x, k1v.y), acc[m][n + 1]);
 #pragma unroll
-      for (int m = 0; m < MR; ++m) s[m][n] = fmaf(qv[m].z, kv.z, s[m][n]);
+        for (int m = 0; m < MR; ++m)
+          acc[m][n] = __ffma2_rn(make_float2(qv[m].z, qv[m].w), make_float2(k0v.z, k0v.w), acc[m][n]);
 #pragma unroll
-      for (int m = 0; m < MR; ++m) s[m][n] = fmaf(qv[m].w, kv.w, s[m][n]);
+        for (int m = 0; m < MR; ++m)
+          acc[m][n + 1] = __ffma2_rn(make_float2(qv[m].z, qv[m].w), make_float2(k1v.z, k1v.w), acc[m][n + 1]);
+      }
+    } else {
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const float4 kv = lds128(ka + n * 8 * 128);
+#pragma unroll
+        for (int m = 0; m < MR; ++m) s[m][n] = fmaf(qv[m].x, kv.x, s[m][n]);
+#pragma unroll
+        for (int m = 0; m < MR; ++m) s[m][n] = fmaf(qv[m].y, kv.y, s[m][n]);
+#pragma unroll
+        for (int m = 0; m < MR; ++m) s[m][n] = fmaf(qv[m].z, kv.z, s[m][n]);
+#pragma unroll
+        for (int m = 0; m < MR; ++m) s[m][n] = fmaf(qv[m].w, kv.w, s[m][n]);
+      }
     }
+  }
+  if constexpr (P2) {
+#pragma unroll
+    for (int m = 0; m < MR; ++m)
+#pragma unroll
+      for (int n = 0; n < 8; ++n) s[m][n] = acc[m][n].x + acc[m][n].y;
   }
 }
 
-// o[m][:] += p[m] * (V row at shared byte address va: columns 4cg..4cg+3 of
-// half 0 and 32+4cg.. of half 1, already swizzled for that row).
-template <int MR>
-__device__ __forceinline__ void pv_row(float (&o)[MR][8], const float (&p)[MR], uint32_t va) {
+// o[m][i] += p[m] * (V row at shared byte address va, columns
+// 4cg + {0,1}, {2,3} of half 0 and 32 + 4cg + {0,1}, {2,3} of half 1, already
+// swizzled for that row).  O is held as column pairs; with P2 each pair is
+// one packed FFMA2 (the same per-element FMA as two FFMAs).
+template <int MR, bool P2>
+__device__ __forceinline__ void pv_row(float2 (&o)[MR][4], const float (&p)[MR], uint32_t va) {
   constexpr uint32_t VH = kBN * kHalfCols * 4;
   const float4 x = lds128(va);
   const float4 y = lds128(va + VH);
+  const float2 v[4] = {make_float2(x.x, x.y), make_float2(x.z, x.w), make_float2(y.x, y.y),
+                       make_float2(y.z, y.w)};
 #pragma unroll
   for (int m = 0; m < MR; ++m) {
-    o[m][0] = fmaf(p[m], x.x, o[m][0]);
-    o[m][1] = fmaf(p[m], x.y, o[m][1]);
-    o[m][2] = fmaf(p[m], x.z, o[m][2]);
-    o[m][3] = fmaf(p[m], x.w, o[m][3]);
-    o[m][4] = fmaf(p[m], y.x, o[m][4]);
-    o[m][5] = fmaf(p[m], y.y, o[m][5]);
-    o[m][6] = fmaf(p[m], y.z, o[m][6]);
-    o[m][7] = fmaf(p[m], y.w, o[m][7]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (P2) {
+        o[m][i] = __ffma2_rn(make_float2(p[m], p[m]), v[i], o[m][i]);
+      } else {
+        o[m][i].x = fmaf(p[m], v[i].x, o[m][i].x);
+        o[m][i].y = fmaf(p[m], v[i].y, o[m][i].y);
+      }
+    }
   }
 }
 
@@ -172,8 +218,8 @@ __device__ __forceinline__ void pv_row(float (&o)[MR][8], const float (&p)[MR], 
 // first P row (row stride 4 rows); v0: shared address of V half 0 row 0 plus
 // (cg << 4).  Keys go 8 at a time (rows 8*j8 + u hold chunk cg at cg ^ u);
 // keys at or past nv (valid_len inside a partial tile) are never read.
-template <int MR>
-__device__ __forceinline__ void pv_tile(float (&o)[MR][8], uint32_t pa, uint32_t v0, int nv) {
+template <int MR, bool P2>
+__device__ __forceinline__ void pv_tile(float2 (&o)[MR][4], uint32_t pa, uint32_t v0, int nv) {
   const int groups = nv >> 3;
 #pragma unroll 1
   for (int j8 = 0; j8 < groups; ++j8) {
@@ -189,7 +235,7 @@ __device__ __forceinline__ void pv_tile(float (&o)[MR][8], uint32_t pa, uint32_t
 #pragma unroll
         for (int m = 0; m < MR; ++m)
           p[m] = jj == 0 ? pv[m].x : jj == 1 ? pv[m].y : jj == 2 ? pv[m].z : pv[m].w;
-        pv_row(o, p, (v0 + (j8 * 8 + u) * 128) ^ static_cast<uint32_t>(u << 4));
+        pv_row<MR, P2>(o, p, (v0 + (j8 * 8 + u) * 128) ^ static_cast<uint32_t>(u << 4));
       }
     }
   }
@@ -198,7 +244,7 @@ __device__ __forceinline__ void pv_tile(float (&o)[MR][8], uint32_t pa, uint32_t
     float p[MR];
 #pragma unroll
     for (int m = 0; m < MR; ++m) p[m] = lds32(pa + (m * 4 * kPS + j) * 4);
-    pv_row(o, p, (v0 + j * 128) ^ static_cast<uint32_t>((j & 7) << 4));
+    pv_row<MR, P2>(o, p, (v0 + j * 128) ^ static_cast<uint32_t>((j & 7) << 4));
   }
 }
 
@@ -242,7 +288,8 @@ constexpr int min_blocks() {
 }
 
 // WARPS warps of RPW (32 or 16) query rows; each lane owns MR = RPW/4 rows.
-template <int WARPS, int RPW, int STAGES, bool TIMED>
+// PQK / PPV: packed FFMA2 in the QK^T / PV tiles.
+template <int WARPS, int RPW, int STAGES, bool PQK, bool PPV, bool TIMED>
 __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
     tiled64_fwd(const __grid_constant__ AttnArgs a, const __grid_constant__ TmaMaps maps) {
   static_assert(RPW == 16 || RPW == 32, "rows per warp");
@@ -325,14 +372,14 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
 
   volatile int* abort_flag = &sm.abort_flag;
   const float qscale = a.qscale;
-  float o[MR][8];
+  float2 o[MR][4];  // column pairs (4cg, 4cg+1), (4cg+2, 4cg+3), (32+4cg, ..), (34+4cg, ..)
   float msc[MR], lrow[MR];
 #pragma unroll
   for (int m = 0; m < MR; ++m) {
     msc[m] = -INFINITY;
     lrow[m] = 0.f;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) o[m][c] = 0.f;
+    for (int c = 0; c < 4; ++c) o[m][c] = make_float2(0.f, 0.f);
   }
 
   const uint32_t q0 = smem_addr(&sm.q[0][warp * kRowsPerWarp + rg][0]);
@@ -354,7 +401,7 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
     float sc[MR][8];
     if (active) {
       clk.tile();
-      qk_tile<MR, kQHalf>(sc, q0, smem_addr(&sm.k[s][0][cg][0]), rg, cg);
+      qk_tile<MR, kQHalf, PQK>(sc, q0, smem_addr(&sm.k[s][0][cg][0]), rg, cg);
       if (!whole) {
         // Per-element mask: key j allowed for row i iff lo(i) <= j < hi(i)
         // (hi <= valid_len, so padded keys are always masked).  Rows past
@@ -405,7 +452,14 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
         }
         lrow[m] = fmaf(lrow[m], alpha, rs);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) o[m][c] *= alpha;
+        for (int c = 0; c < 4; ++c) {
+          if constexpr (PPV) {
+            o[m][c] = __fmul2_rn(o[m][c], make_float2(alpha, alpha));
+          } else {
+            o[m][c].x *= alpha;
+            o[m][c].y *= alpha;
+          }
+        }
       }
     }
     __syncwarp();
@@ -413,7 +467,7 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
 
     if (!mbar_wait_bounded(&sm.vbar[s], par, abort_flag, a.status, a.timeout_cycles)) { ok = false; break; }
     clk.lap(kStageVWait);
-    if (active) pv_tile(o, pa, smem_addr(&sm.v[s][0][0][0]) + (cg << 4), min(kBN, valid - kt));
+    if (active) pv_tile<MR, PPV>(o, pa, smem_addr(&sm.v[s][0][0][0]) + (cg << 4), min(kBN, valid - kt));
     clk.lap(kStagePv);
     if (arrive_last<WARPS>(&sm.vdone[s], lane) && t + STAGES < ntiles && lane == 0) {
       const int y = static_cast<int>(row_base + (t_begin + t + STAGES) * kBN);
@@ -437,8 +491,8 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
       float4 x = make_float4(0.f, 0.f, 0.f, 0.f), y = x;
       if (row < valid) {
         const float inv = l > 0.f ? 1.0f / l : 0.f;
-        x = make_float4(o[m][0] * inv, o[m][1] * inv, o[m][2] * inv, o[m][3] * inv);
-        y = make_float4(o[m][4] * inv, o[m][5] * inv, o[m][6] * inv, o[m][7] * inv);
+        x = make_float4(o[m][0].x * inv, o[m][0].y * inv, o[m][1].x * inv, o[m][1].y * inv);
+        y = make_float4(o[m][2].x * inv, o[m][2].y * inv, o[m][3].x * inv, o[m][3].y * inv);
       }
       float* orow = outp + static_cast<size_t>(row) * kD;
       st_stream(orow + 4 * cg, x);
