@@ -47,8 +47,10 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target CPU work of the cpu_baseline sample")
+    ap.add_argument("--soak", type=float, default=1.0,
+                    help="seconds of untimed steps, clock-sampled, right before the timed region")
     return ap.parse_args()
 
 
@@ -85,7 +87,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", ",".join(str(g) for g in self.gpu_ids)],
+                 "-lms", "50", "-i", ",".join(str(g) for g in self.gpu_ids)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -99,7 +101,6 @@ class ClockSampler:
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -123,7 +124,8 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None,
                 "power_w_max": max(power) if power else None,
-                "samples": len(sm), "reasons": sorted(reasons)}
+                "samples": len(sm), "reasons": sorted(reasons),
+                "window": "1 s soak of the same step + the timed region, 50 ms period"}
 
 
 def load_peaks() -> dict:
@@ -261,10 +263,20 @@ def run_b200(args) -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
+    # Clocks: nvidia-smi samples every 50 ms from the start of an untimed soak
+    # of the same step (about args.soak seconds, so that the samples see the
+    # GPU under this load) through the end of the timed region, which follows
+    # the soak with no gap.
     sampler = ClockSampler(list(range(world)) if rank == 0 else [local])
     if rank == 0:
         sampler.start()
-        time.sleep(0.3)
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < args.soak:
+        for _ in range(10):
+            step()
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     for _ in range(args.steps):
@@ -377,10 +389,14 @@ def cpu_baseline(args, w, q, k, v, valid, dev) -> dict:
     p_all = oracle.Problem(w.batch, H, L, D, mask=oracle.MASK_BLOCK, block=w.block, halo=w.halo)
     pairs_all, _ = oracle.count(p_all, valid)
     # calibrate on one sequence, then size the sample to ~cpu_seconds
+    host = {}
+
     def run(nb):
         ps = oracle.Problem(nb, H, L, D, mask=oracle.MASK_BLOCK, block=w.block, halo=w.halo)
         m = nb * H * L * D
-        qs, ks, vs = (x[:m].cpu().numpy() for x in (q, k, v))
+        if host.get("m") != m:
+            host.update(m=m, x=tuple(x[:m].cpu().numpy() for x in (q, k, v)))
+        qs, ks, vs = host["x"]
         t0 = time.perf_counter()
         oracle.tiled(ps, qs, ks, vs, valid[:nb], threads=threads)
         dt = time.perf_counter() - t0
@@ -388,9 +404,16 @@ def cpu_baseline(args, w, q, k, v, valid, dev) -> dict:
         return 4 * D * pairs / dt / 1e9, dt
     rate, dt1 = run(1)
     nb = int(max(1, min(w.batch, args.cpu_seconds / max(dt1, 1e-3))))
-    rate, dt = run(nb)
+    rates, total, reps = [], 0.0, 0
+    while total < args.cpu_seconds and reps < 200:
+        rate, dt = run(nb)
+        rates.append(rate)
+        total += dt
+        reps += 1
+    rate = statistics.median(rates)
     return {"value": round(rate, 3), "unit": "GFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{nb} of {w.batch} sequences x {H} heads of {w.name} (same inputs), {dt:.1f} s",
+            "sample": f"{nb} of {w.batch} sequences x {H} heads of {w.name} (same inputs), "
+                      f"median of {reps} passes, {total:.1f} s of CPU work",
             "cpu": cpu_model(),
             "what": "C restatement of raya Tiled + AVX2 micro-kernels (oracle/tiled.c)"}
 
