@@ -49,6 +49,12 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target CPU work of the cpu_baseline sample")
+    ap.add_argument("--packed", action="store_true",
+                    help="the caller's layout: packed qkv [B][L][3][H][64] in, context [B][L][H][64] out")
+    ap.add_argument("--rope-theta", type=float, default=0.0,
+                    help="with --packed: raya's rotary embedding on q and k (0 = off)")
+    ap.add_argument("--raya-bench", action="store_true",
+                    help="run raya's local_attention bench shapes and write results/kernel-bench/*.json")
     ap.add_argument("--soak", type=float, default=1.0,
                     help="seconds of untimed steps, clock-sampled, right before the timed region")
     return ap.parse_args()
@@ -253,7 +259,21 @@ def run_b200(args) -> None:
     # in MEASURED_PEAKS.json), measured before the timed region.
     ffma_tflops = rb.ffma_peak(5)
 
+    if args.packed:
+        # The same numbers laid out as the encoder's packed projection.
+        packed = []
+        for lq, lk, lv, lo in layers:
+            qkv = torch.stack([t.view(w.batch, w.heads, w.seq, D).transpose(1, 2) for t in (lq, lk, lv)],
+                              dim=2).contiguous().view(-1)
+            packed.append((qkv, torch.empty_like(lo)))
+        ws = torch.empty(w.seq * 64, dtype=torch.float32, device=dev) if args.rope_theta > 0 else None
+
     def step():
+        if args.packed:
+            for qkv, ctx in packed:
+                kern.attend_packed(shape, params, qkv, ctx, valid_len=dvalid, rope_theta=args.rope_theta or None,
+                                   workspace=ws, stream=stream)
+            return
         for lq, lk, lv, lo in layers:  # layers back to back on one stream
             kern.attend_device(shape, params, lq, lk, lv, lo, valid_len=dvalid, stream=stream)
 
@@ -318,7 +338,7 @@ def run_b200(args) -> None:
 
     # End to end through the host-buffer API (pinned inputs, synchronous).
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and not args.packed:
         hq, hk, hv, ho = (torch.empty(n, dtype=torch.float32).pin_memory() for _ in range(4))
         for h, d in zip((hq, hk, hv), (q, k, v)):
             h.copy_(d)
@@ -347,13 +367,13 @@ def run_b200(args) -> None:
     # Stage proportions of one extra, instrumented launch (the reference
     # bench's "stages" field, benches/local_attention.rs:127-130,155-157).
     stages = None
-    if args.kernel != 2:
+    if args.kernel != 2 and not args.packed:
         st = rb.stage_times(shape, params, q, k, v, out, valid_len=dvalid,
                             kernel=args.kernel or rb.KERNEL_TILED64)
         stages = {key: round(val, 2) for key, val in st.items() if key.endswith("pct")}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.packed:
         cpu = cpu_baseline(args, w, q, k, v, valid, dev)
 
     if world > 1:
@@ -370,6 +390,8 @@ def run_b200(args) -> None:
         "queries_per_s": round(qps, 1),
         "frac_fp32_peak": roofline["frac"],
         "gpu_launches": args.steps * w.layers,
+        "layout": ("packed qkv -> context" + (f", rope theta {args.rope_theta:g}" if args.rope_theta else "")
+                   if args.packed else "head-major q, k, v -> out"),
         "kernel": "rowwise (raya_b200/csrc/rowwise.cuh)" if args.kernel == 2 else
                   f"tiled64 (raya_b200/csrc/tiled64.cuh), kernel id {args.kernel or 1}",
         "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "stages": stages,
@@ -418,8 +440,45 @@ def cpu_baseline(args, w, q, k, v, valid, dev) -> dict:
             "what": "C restatement of raya Tiled + AVX2 micro-kernels (oracle/tiled.c)"}
 
 
+def raya_bench(args) -> None:
+    """raya's local_attention bench on the GPU (raya_b200/kernel_bench.py),
+    with the CPU baseline rows of the same file: the Tiled + AVX2 restatement
+    at 1 thread and at every host thread, like the reference bench's tiled
+    rows (benches/local_attention.rs:114-140)."""
+    from raya_b200 import kernel_bench
+
+    threads = host_threads()
+
+    def cpu_rows(seq, mask, q, k, v):
+        import oracle
+
+        m = (dict(mask=oracle.MASK_BLOCK, block=128, halo=1) if mask == "block3"
+             else dict(mask=oracle.MASK_WINDOW, window=64))
+        p = oracle.Problem(1, kernel_bench.HEADS, seq, kernel_bench.HEAD_DIM, **m)
+        qh, kh, vh = (x.cpu().numpy() for x in (q, k, v))
+        rows = []
+        for t in sorted({1, threads}):
+            times = []
+            for _ in range(3):
+                t0 = time.perf_counter()
+                oracle.tiled(p, qh, kh, vh, threads=t)
+                times.append((time.perf_counter() - t0) * 1e3)
+            rows.append({"kernel": "tiled", "mask": mask, "backend": "avx2", "seq": seq,
+                         "heads": kernel_bench.HEADS, "head_dim": kernel_bench.HEAD_DIM, "threads": t,
+                         "mean_ms": statistics.mean(times), "stddev_ms": statistics.stdev(times),
+                         "samples": len(times),
+                         "note": "C restatement of raya Tiled + AVX2 (oracle/tiled.c), CPU baseline"})
+        return rows
+
+    path = kernel_bench.run(ROOT, None if args.no_cpu_baseline else cpu_rows)
+    print(json.dumps({"raya_bench": path}), flush=True)
+
+
 def main():
     args = parse()
+    if args.raya_bench:
+        raya_bench(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -125,6 +125,26 @@ raya_attn_status raya_attn_forward_ex(const raya_attn_desc* desc, const float* q
                                       const int32_t* valid_len, void* stream,
                                       int kernel_id);
 
+/* The caller's layout, fused (§ "next" of the path: encoder.rs:34-92).
+ * raya's encoder splits a packed projection qkv[seq][3][heads][head_dim] into
+ * head-major q, k, v (split_qkv, encoder.rs:34-53), applies its rotary
+ * embedding to q and k (ops.rs:110-141) and transposes the head-major output
+ * back to ctx[seq][heads*head_dim] (encoder.rs:82-90).  This call does all of
+ * it inside the attention kernel: qkv is the DEVICE tensor
+ * [batch][seq][3][heads][64] (read in place by TMA), ctx the DEVICE tensor
+ * [batch][seq][heads][64] it writes (padded rows +0.0f), valid_len a DEVICE
+ * int32[batch] or NULL.  rope_theta > 0 rotates q and k first (angles in f32
+ * as the reference computes them); 0 skips the rotation.  With rope_theta > 0
+ * the call needs a DEVICE workspace of raya_attn_packed_workspace bytes (the
+ * cos/sin table, written by the call); it may be NULL otherwise.  head_dim
+ * must be 64.  Asynchronous on `stream`; allocates nothing. */
+raya_attn_status raya_attn_forward_packed(const raya_attn_desc* desc, const float* qkv, float* ctx,
+                                          const int32_t* valid_len, float rope_theta, void* workspace,
+                                          size_t workspace_bytes, void* stream);
+
+/* Workspace bytes raya_attn_forward_packed needs for this shape and theta. */
+raya_attn_status raya_attn_packed_workspace(const raya_attn_desc* desc, float rope_theta, size_t* bytes);
+
 /* Stage timing, the counterpart of Tiled::attend_with_stages / StageTimes
  * (tiled/mod.rs:60-126, tiled/stages.rs:1-31): raya_attn_forward_ex with a
  * tiled kernel (kernel_id AUTO, TILED64 or a TILED64_* variant) whose warps

@@ -106,6 +106,10 @@ def lib():
         L.oracle_rand_vec.argtypes = [fp, ctypes.c_size_t, ctypes.c_uint64]
         L.oracle_lcg_fill.argtypes = [fp, ctypes.c_size_t, ctypes.c_uint32]
         L.oracle_cpu_has_avx2_fma.restype = ctypes.c_int
+        i64 = ctypes.c_int64
+        L.oracle_split_qkv.argtypes = [fp, i64, i64, i64, fp, fp, fp]
+        L.oracle_rope_inplace.argtypes = [fp, i64, i64, i64, ctypes.c_float]
+        L.oracle_merge_ctx.argtypes = [fp, i64, i64, i64, fp]
         _lib = L
     return _lib
 
@@ -228,3 +232,28 @@ def dense_reference(p: Problem, q, k, v, valid_len=None) -> np.ndarray:
             w = np.divide(e, tot[:, None], out=np.zeros_like(e), where=tot[:, None] > 0)
             out[b, h] = w @ v4[b, h]
     return out.reshape(-1)
+
+
+def encoder_attend(qkv: np.ndarray, batch: int, seq: int, heads: int, head_dim: int, mask: int,
+                   block: int, halo: int, window: int, valid_len, rope_theta: float | None) -> np.ndarray:
+    """The caller's whole attention step, restated: per batch entry,
+    split_qkv (encoder.rs:34-53), rope on q and k (ops.rs:110-141) when
+    rope_theta is given, Naive attention, and the context back to
+    [seq][heads*head_dim] (encoder.rs:82-90).  Returns ctx
+    [batch][seq][heads*head_dim]."""
+    L = lib()
+    n = seq * heads * head_dim
+    ctx = np.zeros(batch * n, dtype=np.float32)
+    p = Problem(1, heads, seq, head_dim, mask=mask, block=block, halo=halo, window=window)
+    for b in range(batch):
+        src = np.ascontiguousarray(qkv[b * 3 * n:(b + 1) * 3 * n])
+        q, k, v = (np.empty(n, dtype=np.float32) for _ in range(3))
+        L.oracle_split_qkv(_f32(src), seq, heads, head_dim, _f32(q), _f32(k), _f32(v))
+        if rope_theta:
+            L.oracle_rope_inplace(_f32(q), heads, seq, head_dim, rope_theta)
+            L.oracle_rope_inplace(_f32(k), heads, seq, head_dim, rope_theta)
+        out = naive(p, q, k, v, [int(np.broadcast_to(valid_len, (batch,))[b])])
+        part = np.empty(n, dtype=np.float32)
+        L.oracle_merge_ctx(_f32(out), seq, heads, head_dim, _f32(part))
+        ctx[b * n:(b + 1) * n] = part
+    return ctx

@@ -76,6 +76,15 @@ int oracle_cpu_has_avx2_fma(void);
 void oracle_count(const oracle_desc* d, const int32_t* valid_len,
                   uint64_t* pairs, uint64_t* rows);
 
+/* The caller's layout transforms (encoder.c): split a packed [seq][3][heads]
+ * [head_dim] projection into head-major q, k, v (encoder.rs:34-53); raya's
+ * rotary embedding in place on [heads][seq][head_dim] (ops.rs:110-141); the
+ * head-major output back to [seq][heads*head_dim] (encoder.rs:82-90). */
+void oracle_split_qkv(const float* qkv, int64_t seq, int64_t heads, int64_t head_dim, float* q,
+                      float* k, float* v);
+void oracle_rope_inplace(float* x, int64_t heads, int64_t seq, int64_t head_dim, float theta);
+void oracle_merge_ctx(const float* out, int64_t seq, int64_t heads, int64_t head_dim, float* ctx);
+
 /* tests/common/mod.rs:6-18: xorshift values uniform in [-1, 1]. */
 void oracle_rand_vec(float* out, size_t n, uint64_t seed);
 

@@ -302,6 +302,35 @@ class Cuda(AttentionKernel):
         if keep is not None:  # keep the uploaded lengths alive until the kernel has run
             _sync(stream)
 
+    def attend_packed(self, shape: AttnShape, params: AttnParams, qkv, ctx, valid_len=None,
+                      rope_theta: float | None = None, workspace=None, stream=None) -> None:
+        """The encoder's attention step in its own layout (encoder.rs:57-92):
+        qkv is the packed projection [batch][seq][3][heads][64] and ctx the
+        context [batch][seq][heads][64], both CUDA float32 tensors; with
+        rope_theta, q and k get raya's rotary embedding (ops.rs:110-141)
+        first.  Asynchronous on ``stream``."""
+        import torch
+
+        d = make_desc(shape, params)
+        theta = float(rope_theta or 0.0)
+        need = ctypes.c_size_t()
+        _check(lib.raya_attn_packed_workspace(ctypes.byref(d), theta, ctypes.byref(need)))
+        if workspace is None and need.value:
+            workspace = torch.empty(need.value // 4, dtype=torch.float32, device=qkv.device)
+        keep = valid_len
+        if keep is None:
+            keep = torch.from_numpy(params.valid_array(shape.batch)).to(qkv.device)
+        if stream is None:
+            stream = torch.cuda.current_stream(qkv.device).cuda_stream
+        elif isinstance(stream, torch.cuda.Stream):
+            stream = stream.cuda_stream
+        ws_ptr = workspace.data_ptr() if workspace is not None else None
+        ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        _check(lib.raya_attn_forward_packed(ctypes.byref(d), qkv.data_ptr(), ctx.data_ptr(), keep.data_ptr(),
+                                            theta, ws_ptr, ws_bytes, stream))
+        if valid_len is None or workspace is not None:
+            _sync(stream)  # uploaded lengths / the caller's workspace stay valid until done
+
 
 STAGE_NAMES = ("qk", "softmax", "pv", "k_wait", "v_wait", "refill", "tiles", "total")
 

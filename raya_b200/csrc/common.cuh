@@ -32,6 +32,7 @@ struct AttnArgs {
   int row_tiles;      // CTA row tiles per (batch, head) slice
   long long timeout_cycles;  // bound of every spin wait
   unsigned long long* stage_cycles;  // device [kStageSlots] or nullptr (timed kernels only)
+  const float* rope_cs;  // device [seq][head_dim/2] of (cos, sin), rotary kernels only
 };
 
 // Stage-timing slots (the counterpart of StageTimes, tiled/stages.rs:1-31):
@@ -158,6 +159,15 @@ __device__ __forceinline__ float4 lds128(uint32_t addr) {
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                : "r"(addr));
   return v;
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 __device__ __forceinline__ float lds32(uint32_t addr) {

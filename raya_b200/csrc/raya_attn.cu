@@ -56,6 +56,24 @@ const TiledVariant kTiled[] = {
     variant<4, 16, 1, true, true>(RAYA_KERNEL_TILED64_W4R16_P2),
     variant<4, 32, 1, false, true>(RAYA_KERNEL_TILED64_W4R32_P2)};
 
+// The packed-layout (caller's [b*seq][3][heads][64] -> [b*seq][heads][64])
+// instantiations of the two tuned variants, without and with rotary embedding.
+struct PackedVariant {
+  int id;
+  int warps;
+  int rows_per_warp;
+  TiledFn plain;
+  TiledFn rope;
+  size_t smem;
+};
+template <int W, int R, bool PQK, bool PPV>
+constexpr PackedVariant packed_variant(int id) {
+  return {id, W, R, tiled64::tiled64_fwd<W, R, 1, PQK, PPV, false, tiled64::kPacked, false>,
+          tiled64::tiled64_fwd<W, R, 1, PQK, PPV, false, tiled64::kPacked, true>, tiled64::smem_bytes<W, R, 1>()};
+}
+const PackedVariant kPacked[] = {packed_variant<4, 16, true, true>(RAYA_KERNEL_TILED64_W4R16_P2),
+                                 packed_variant<4, 32, false, true>(RAYA_KERNEL_TILED64_W4R32_P2)};
+
 // The tuned choice (measured on B200, profiles/): 64-row CTAs of 16-row warps
 // with packed QK^T and PV for short key spans (block <= 64, windows), 128-row
 // CTAs of 32-row warps with packed PV for long ones (block >= 128, Full).
@@ -122,6 +140,13 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tiled64 smem)");
       }
     }
+    for (const PackedVariant& pv : kPacked) {
+      for (auto fn : {pv.plain, pv.rope}) {
+        e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pv.smem));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(packed smem)");
+      }
+    }
     c.ready = true;
   }
   *out = &c;
@@ -130,7 +155,7 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
 
 // A 2-D tensor map over a [rows][64] fp32 tensor with boxes of
 // [box_rows][32 floats], 128-byte swizzle, zero fill out of bounds.
-raya_attn_status encode_rows64(CUtensorMap* map, const float* base, uint64_t rows, uint32_t box_rows) {
+raya_attn_status load_encoder() {
   std::call_once(g_encode_once, [] {
     cudaDriverEntryPointQueryResult q;
     void* fn = nullptr;
@@ -139,6 +164,12 @@ raya_attn_status encode_rows64(CUtensorMap* map, const float* base, uint64_t row
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   });
   if (!g_encode) return fail(RAYA_ATTN_ERR_CUDA, "cuda: cuTensorMapEncodeTiled is unavailable");
+  return RAYA_ATTN_OK;
+}
+
+raya_attn_status encode_rows64(CUtensorMap* map, const float* base, uint64_t rows, uint32_t box_rows) {
+  raya_attn_status st = load_encoder();
+  if (st != RAYA_ATTN_OK) return st;
   const cuuint64_t gdim[2] = {64, rows};
   const cuuint64_t gstride[1] = {64 * sizeof(float)};
   const cuuint32_t box[2] = {32, box_rows};
@@ -148,6 +179,24 @@ raya_attn_status encode_rows64(CUtensorMap* map, const float* base, uint64_t row
                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(RAYA_ATTN_ERR_CUDA, "cuda: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return RAYA_ATTN_OK;
+}
+
+// A 4-D tensor map over the packed projection [rows][3][heads][64] fp32
+// (rows = batch*seq) with boxes of [box_rows][1][1][32 floats]: one head of
+// one of q/k/v at box_rows consecutive positions, 128-byte swizzle.
+raya_attn_status encode_packed(CUtensorMap* map, const float* base, uint64_t rows, uint64_t heads,
+                               uint32_t box_rows) {
+  raya_attn_status st = load_encoder();
+  if (st != RAYA_ATTN_OK) return st;
+  const cuuint64_t gdim[4] = {64, heads, 3, rows};
+  const cuuint64_t gstride[3] = {64 * sizeof(float), heads * 64 * sizeof(float), 3 * heads * 64 * sizeof(float)};
+  const cuuint32_t box[4] = {32, 1, 1, box_rows};
+  const cuuint32_t estride[4] = {1, 1, 1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), gdim, gstride,
+                              box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(RAYA_ATTN_ERR_CUDA, "cuda: cuTensorMapEncodeTiled (packed) failed (%d)", static_cast<int>(r));
   return RAYA_ATTN_OK;
 }
 
@@ -347,6 +396,19 @@ __global__ void __launch_bounds__(256) ffma_probe_kernel(float* sink, int iters,
   if (s == 1234.5f) sink[blockIdx.x * blockDim.x + threadIdx.x] = s;
 }
 
+// raya's rotary table (ops.rs:118-131): cs[pos][i] = (cos, sin) of
+// angle = pos * inv_freq[i] in f32, inv_freq computed on the host with the C
+// library's powf exactly as the reference computes it.
+struct RopeFreq {
+  float inv_freq[32];
+};
+__global__ void rope_table_kernel(float2* cs, int seq, const __grid_constant__ RopeFreq f) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= seq * 32) return;
+  const float angle = __fmul_rn(static_cast<float>(idx >> 5), f.inv_freq[idx & 31]);
+  cs[idx] = make_float2(cosf(angle), sinf(angle));
+}
+
 // Failure-detection probe: one warp waits on an mbarrier that nothing ever
 // arrives on, through the same bounded wait the attention kernels use, with a
 // short limit.  The wait gives up, records bit 0 of the status word and the
@@ -413,6 +475,72 @@ raya_attn_status raya_attn_forward_timed(const raya_attn_desc* desc, const float
   if (kernel_id == RAYA_KERNEL_AUTO) kernel_id = RAYA_KERNEL_TILED64;
   return launch(desc, q, k, v, out, valid_len, static_cast<cudaStream_t>(stream), kernel_id,
                 reinterpret_cast<unsigned long long*>(stage_cycles));
+}
+
+raya_attn_status raya_attn_packed_workspace(const raya_attn_desc* desc, float rope_theta, size_t* bytes) {
+  raya_attn_status st = check_shape(desc);
+  if (st != RAYA_ATTN_OK) return st;
+  if (!bytes) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null output");
+  *bytes = rope_theta > 0.f ? static_cast<size_t>(desc->seq) * 32 * 2 * sizeof(float) : 0;
+  return RAYA_ATTN_OK;
+}
+
+raya_attn_status raya_attn_forward_packed(const raya_attn_desc* desc, const float* qkv, float* ctx,
+                                          const int32_t* valid_len, float rope_theta, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  raya_attn_status st = check_shape(desc);
+  if (st != RAYA_ATTN_OK) return st;
+  if (desc->head_dim != 64)
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the packed layout needs head_dim 64, got %lld",
+                static_cast<long long>(desc->head_dim));
+  if (!std::isfinite(rope_theta) || rope_theta < 0.f)
+    return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: rope_theta %g", static_cast<double>(rope_theta));
+  if (desc->seq == 0) return RAYA_ATTN_OK;
+  if (!qkv || !ctx) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null tensor pointer");
+  if (!aligned16(qkv) || !aligned16(ctx) || (workspace && !aligned16(workspace)))
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: tensors must be 16-byte aligned");
+  const bool rope = rope_theta > 0.f;
+  size_t need = 0;
+  raya_attn_packed_workspace(desc, rope_theta, &need);
+  if (rope && (!workspace || workspace_bytes < need))
+    return fail(RAYA_ATTN_ERR_LENGTH, "buffer `workspace` has length %zu, expected %zu", workspace_bytes, need);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DeviceCtx* ctx_dev = nullptr;
+  st = ensure_ready(dev, &ctx_dev);
+  if (st != RAYA_ATTN_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rope) {
+    RopeFreq f;
+    for (int i = 0; i < 32; ++i)  // ops.rs:120-122, in f32 with the C library's powf
+      f.inv_freq[i] = 1.0f / powf(rope_theta, static_cast<float>(2 * i) / 64.0f);
+    const int n = static_cast<int>(desc->seq) * 32;
+    rope_table_kernel<<<(n + 255) / 256, 256, 0, s>>>(static_cast<float2*>(workspace), static_cast<int>(desc->seq), f);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "rope table launch");
+  }
+  const int id = tuned_tiled(desc);
+  const PackedVariant* pv = nullptr;
+  for (const PackedVariant& v : kPacked)
+    if (v.id == id) pv = &v;
+  const int bm = pv->warps * pv->rows_per_warp;
+  AttnArgs a = make_args(desc, qkv, qkv, qkv, ctx, valid_len, ctx_dev->status);
+  a.rope_cs = rope ? static_cast<const float*>(workspace) : nullptr;
+  a.row_tiles = static_cast<int>((desc->seq + bm - 1) / bm);
+  const long long grid = static_cast<long long>(desc->batch) * desc->heads * a.row_tiles;
+  if (grid > 0x7fffffffll)
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
+  tiled64::TmaMaps maps;
+  const uint64_t rows = static_cast<uint64_t>(desc->batch) * desc->seq;
+  st = encode_packed(&maps.q, qkv, rows, desc->heads, static_cast<uint32_t>(bm));
+  if (st == RAYA_ATTN_OK) st = encode_packed(&maps.k, qkv, rows, desc->heads, tiled64::kBN);
+  if (st != RAYA_ATTN_OK) return st;
+  maps.v = maps.k;
+  (rope ? pv->rope : pv->plain)<<<static_cast<unsigned>(grid), pv->warps * 32, pv->smem, s>>>(a, maps);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "packed kernel launch");
+  return RAYA_ATTN_OK;
 }
 
 raya_attn_status raya_attn_probe_timeout(int64_t timeout_cycles, void* stream) {

@@ -54,6 +54,7 @@ struct Smem {
   uint64_t qbar;
   uint64_t kbar[STAGES];
   uint64_t vbar[STAGES];
+  uint64_t kready[STAGES];  // rotary kernels: every warp has rotated its part of K
   int kdone[STAGES];
   int vdone[STAGES];
   int kissued[STAGES];
@@ -79,14 +80,70 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            int w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Tensor layouts the kernel reads and writes.
+//   kHeadMajor: q, k, v, out are [batch*heads*seq][64] (raya's [heads][seq][head_dim]
+//               per batch entry); 2-D tensor maps, coordinates (column, slice*seq + pos).
+//   kPacked:    q, k, v are the packed projection [batch*seq][3][heads][64]
+//               (encoder.rs:34-53 before split_qkv); 4-D tensor maps, coordinates
+//               (column, head, which, b*seq + pos); out is the context
+//               [batch*seq][heads][64] (encoder.rs:82-90 after the transpose back).
+enum Layout : int { kHeadMajor = 0, kPacked = 1 };
+
 // One thread: post the byte count of a [rows x 64] tile and issue its two
-// column-half boxes.
+// column-half boxes (`which` selects q/k/v in the packed layout).
+template <int LAYOUT>
 __device__ __forceinline__ void stage_tile(float* half0, float* half1, const CUtensorMap* map,
-                                           int y, int rows, uint64_t* bar) {
+                                           int head, int which, int y, int rows, uint64_t* bar) {
   fence_proxy_async_smem();
   mbar_arrive_expect_tx(bar, static_cast<uint32_t>(rows) * kD * 4);
-  tma_load_2d(half0, map, 0, y, bar);
-  tma_load_2d(half1, map, kHalfCols, y, bar);
+  if constexpr (LAYOUT == kHeadMajor) {
+    tma_load_2d(half0, map, 0, y, bar);
+    tma_load_2d(half1, map, kHalfCols, y, bar);
+  } else {
+    tma_load_4d(half0, map, 0, head, which, y, bar);
+    tma_load_4d(half1, map, kHalfCols, head, which, y, bar);
+  }
+}
+
+// raya's rotary embedding (ops.rs:110-141, rotate-half form) on rows
+// [r0, r0 + nrows) of a staged [rows][64] tile whose row r holds position
+// pos0 + r: element i and i + 32 of a row become a*cos - b*sin and
+// b*cos + a*sin, with (cos, sin) of that position and i from the table
+// cs[pos][32][2], in unfused f32 arithmetic as the reference computes it.
+// Rows at or past `valid` are left as they are (their keys are masked and
+// their outputs are zero).  Warp-collective; the caller synchronises.
+__device__ __forceinline__ void rope_rows(uint32_t half0, uint32_t half1, int r0, int nrows, int pos0,
+                                          int valid, const float* __restrict__ cs, int lane) {
+  for (int idx = lane; idx < nrows * 8; idx += 32) {
+    const int r = r0 + (idx >> 3), ch = idx & 7;
+    const int pos = pos0 + r;
+    if (pos >= valid) continue;
+    const uint32_t off = static_cast<uint32_t>(r * 128 + ((ch ^ (r & 7)) << 4));
+    float4 a = lds128(half0 + off), b = lds128(half1 + off);
+    const float4* t = reinterpret_cast<const float4*>(cs + (static_cast<size_t>(pos) * 32 + 4 * ch) * 2);
+    const float4 t0 = __ldg(t), t1 = __ldg(t + 1);  // (cos, sin) of i = 4ch .. 4ch+3
+    auto rot = [](float& x, float& y, float c, float sn) {
+      const float nx = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
+      const float ny = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+      x = nx;
+      y = ny;
+    };
+    rot(a.x, b.x, t0.x, t0.y);
+    rot(a.y, b.y, t0.z, t0.w);
+    rot(a.z, b.z, t1.x, t1.y);
+    rot(a.w, b.w, t1.z, t1.w);
+    sts128(half0 + off, a);
+    sts128(half1 + off, b);
+  }
 }
 
 __device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
@@ -288,8 +345,10 @@ constexpr int min_blocks() {
 }
 
 // WARPS warps of RPW (32 or 16) query rows; each lane owns MR = RPW/4 rows.
-// PQK / PPV: packed FFMA2 in the QK^T / PV tiles.
-template <int WARPS, int RPW, int STAGES, bool PQK, bool PPV, bool TIMED>
+// PQK / PPV: packed FFMA2 in the QK^T / PV tiles.  LAYOUT: Layout above.
+// ROPE: rotate q and k in shared memory before use (packed layout).
+template <int WARPS, int RPW, int STAGES, bool PQK, bool PPV, bool TIMED, int LAYOUT = kHeadMajor,
+          bool ROPE = false>
 __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
     tiled64_fwd(const __grid_constant__ AttnArgs a, const __grid_constant__ TmaMaps maps) {
   static_assert(RPW == 16 || RPW == 32, "rows per warp");
@@ -313,14 +372,20 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
   int valid = a.valid_len ? a.valid_len[b] : seq;
   valid = valid < 0 ? 0 : (valid > seq ? seq : valid);
   const int r0 = tile * kBM;
-  const long long row_base = bh * seq;  // first row of this slice in the [rows][64] view
-  float* __restrict__ outp = a.out + static_cast<size_t>(row_base) * kD;
+  const int head = static_cast<int>(bh - static_cast<long long>(b) * a.heads);
+  // First TMA row of this slice: slice*seq (head-major) or b*seq (packed).
+  const long long row_base = LAYOUT == kHeadMajor ? bh * seq : static_cast<long long>(b) * seq;
+  // Output row `pos` of this slice lives at outp + pos * ostride floats.
+  const size_t ostride = LAYOUT == kHeadMajor ? static_cast<size_t>(kD) : static_cast<size_t>(a.heads) * kD;
+  float* __restrict__ outp = a.out + (LAYOUT == kHeadMajor ? static_cast<size_t>(row_base) * kD
+                                                           : static_cast<size_t>(row_base) * ostride +
+                                                                 static_cast<size_t>(head) * kD);
 
   if (r0 >= valid) {  // the whole tile is padding: exact zeros, no loads
     const int rows = min(kBM, seq - r0);
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int idx = tid; idx < rows * 16; idx += kThreads)
-      st_stream(outp + static_cast<size_t>(r0 + (idx >> 4)) * kD + (idx & 15) * 4, zero);
+      st_stream(outp + static_cast<size_t>(r0 + (idx >> 4)) * ostride + (idx & 15) * 4, zero);
     return;
   }
 
@@ -348,6 +413,7 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&sm.kbar[s], 1);
       mbar_init(&sm.vbar[s], 1);
+      mbar_init(&sm.kready[s], WARPS);
       sm.kdone[s] = sm.vdone[s] = 0;
       sm.kissued[s] = sm.vissued[s] = 0;
     }
@@ -357,13 +423,14 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
   __syncthreads();
 
   if (tid == 0) {
-    stage_tile(&sm.q[0][0][0], &sm.q[1][0][0], &maps.q, static_cast<int>(row_base + r0), kBM, &sm.qbar);
+    stage_tile<LAYOUT>(&sm.q[0][0][0], &sm.q[1][0][0], &maps.q, head, 0, static_cast<int>(row_base + r0), kBM,
+                       &sm.qbar);
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) {
       if (s < ntiles) {
         const int y = static_cast<int>(row_base + (t_begin + s) * kBN);
-        stage_tile(&sm.k[s][0][0][0], &sm.k[s][1][0][0], &maps.k, y, kBN, &sm.kbar[s]);
-        stage_tile(&sm.v[s][0][0][0], &sm.v[s][1][0][0], &maps.v, y, kBN, &sm.vbar[s]);
+        stage_tile<LAYOUT>(&sm.k[s][0][0][0], &sm.k[s][1][0][0], &maps.k, head, 1, y, kBN, &sm.kbar[s]);
+        stage_tile<LAYOUT>(&sm.v[s][0][0][0], &sm.v[s][1][0][0], &maps.v, head, 2, y, kBN, &sm.vbar[s]);
         sm.kissued[s] = 1;
         sm.vissued[s] = 1;
       }
@@ -388,6 +455,13 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
   StageClock<TIMED> clk;
   clk.start();
   bool ok = mbar_wait_bounded(&sm.qbar, 0, abort_flag, a.status, a.timeout_cycles);
+  if constexpr (ROPE) {
+    // Each warp rotates its own query rows, then reads only those.
+    if (ok)
+      rope_rows(smem_addr(&sm.q[0][0][0]), smem_addr(&sm.q[1][0][0]), warp * kRowsPerWarp, kRowsPerWarp, r0,
+                valid, a.rope_cs, lane);
+    __syncwarp();
+  }
 
   for (int t = 0; ok && t < ntiles; ++t) {
     const int s = STAGES == 1 ? 0 : t % STAGES;
@@ -397,6 +471,16 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
     const bool whole = lo_l <= kt && hi_f >= kt + kBN;
 
     if (!mbar_wait_bounded(&sm.kbar[s], par, abort_flag, a.status, a.timeout_cycles)) { ok = false; break; }
+    if constexpr (ROPE) {
+      // The K tile is shared: each warp rotates kBN/WARPS of its rows, then
+      // all warps wait until every part is rotated.
+      constexpr int kRot = kBN / WARPS;
+      rope_rows(smem_addr(&sm.k[s][0][0][0]), smem_addr(&sm.k[s][1][0][0]), warp * kRot, kRot, kt, valid,
+                a.rope_cs, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.kready[s]);
+      if (!mbar_wait_bounded(&sm.kready[s], par, abort_flag, a.status, a.timeout_cycles)) { ok = false; break; }
+    }
     clk.lap(kStageKWait);
     float sc[MR][8];
     if (active) {
@@ -424,7 +508,7 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
     // Done reading K buffer s: the last warp refills it with tile t+STAGES.
     if (arrive_last<WARPS>(&sm.kdone[s], lane) && t + STAGES < ntiles && lane == 0) {
       const int y = static_cast<int>(row_base + (t_begin + t + STAGES) * kBN);
-      stage_tile(&sm.k[s][0][0][0], &sm.k[s][1][0][0], &maps.k, y, kBN, &sm.kbar[s]);
+      stage_tile<LAYOUT>(&sm.k[s][0][0][0], &sm.k[s][1][0][0], &maps.k, head, 1, y, kBN, &sm.kbar[s]);
       sm.kissued[s] += 1;
     }
     clk.lap(kStageRefill);
@@ -471,7 +555,7 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
     clk.lap(kStagePv);
     if (arrive_last<WARPS>(&sm.vdone[s], lane) && t + STAGES < ntiles && lane == 0) {
       const int y = static_cast<int>(row_base + (t_begin + t + STAGES) * kBN);
-      stage_tile(&sm.v[s][0][0][0], &sm.v[s][1][0][0], &maps.v, y, kBN, &sm.vbar[s]);
+      stage_tile<LAYOUT>(&sm.v[s][0][0][0], &sm.v[s][1][0][0], &maps.v, head, 2, y, kBN, &sm.vbar[s]);
       sm.vissued[s] += 1;
     }
     clk.lap(kStageRefill);
@@ -494,7 +578,7 @@ __global__ void __launch_bounds__(WARPS * 32, min_blocks<WARPS, RPW, STAGES>())
         x = make_float4(o[m][0].x * inv, o[m][0].y * inv, o[m][1].x * inv, o[m][1].y * inv);
         y = make_float4(o[m][2].x * inv, o[m][2].y * inv, o[m][3].x * inv, o[m][3].y * inv);
       }
-      float* orow = outp + static_cast<size_t>(row) * kD;
+      float* orow = outp + static_cast<size_t>(row) * ostride;
       st_stream(orow + 4 * cg, x);
       st_stream(orow + 32 + 4 * cg, y);
     }

@@ -142,3 +142,21 @@ def test_shard_rejects_bad_ranks():
     for world, rank in ((0, 0), (2, 2), (2, -1)):
         with pytest.raises(rb.ShapeError):
             rb.shard(shape, params, world, rank)
+
+
+def test_packed_call_validates_on_the_host():
+    import ctypes
+
+    shape = _shape(heads=2, seq=128, d=64, batch=1)
+    d = rb.make_desc(shape, rb.AttnParams.new(rb.Mask.BLOCK3, 128, 64))
+    need = ctypes.c_size_t()
+    assert _lib.lib.raya_attn_packed_workspace(ctypes.byref(d), ctypes.c_float(10000.0), ctypes.byref(need)) == 0
+    assert need.value == 128 * 32 * 2 * 4
+    assert _lib.lib.raya_attn_packed_workspace(ctypes.byref(d), ctypes.c_float(0.0), ctypes.byref(need)) == 0
+    assert need.value == 0
+    # rotation without a workspace: the reference's Length error kind
+    st = _lib.lib.raya_attn_forward_packed(ctypes.byref(d), 16, 16, None, ctypes.c_float(10000.0), None, 0, None)
+    assert st == _lib.ERR_LENGTH and "workspace" in _lib.last_error()
+    bad = rb.make_desc(_shape(heads=2, seq=128, d=32, batch=1), rb.AttnParams.new(rb.Mask.BLOCK3, 128, 32))
+    assert _lib.lib.raya_attn_forward_packed(ctypes.byref(bad), 16, 16, None, ctypes.c_float(0.0), None, 0,
+                                             None) == _lib.ERR_UNSUPPORTED
