@@ -145,6 +145,23 @@ raya_attn_status raya_attn_forward_packed(const raya_attn_desc* desc, const floa
 /* Workspace bytes raya_attn_forward_packed needs for this shape and theta. */
 raya_attn_status raya_attn_packed_workspace(const raya_attn_desc* desc, float rope_theta, size_t* bytes);
 
+/* raya_attn_forward_packed without a workspace: nothing is allocated.  No
+ * counterpart in the reference.  For callers that cannot allocate device
+ * memory: a serving runtime that owns all of the GPU's memory through its
+ * own pool, a binding that only receives raw device pointers from its host,
+ * or a latency-bound loop where cudaMalloc (which may synchronise the
+ * device) must not run.  The rotary cos/sin table lives in a built-in device
+ * array of 8192 positions (2 MiB, held on every GPU that loads the library
+ * until the process exits); with rope_theta > 0 a seq above 8192 is
+ * rejected with RAYA_ATTN_ERR_UNSUPPORTED.  The first call on each device
+ * looks the array's address up (cudaGetSymbolAddress) with that device
+ * current, so make that first call before any stream capture.  All calls
+ * share the array: each rewrites the positions it reads, but calls whose
+ * work overlaps on the GPU (other streams, other host threads) race on it.
+ * Arguments and results as raya_attn_forward_packed. */
+raya_attn_status raya_attn_forward_packed_noalloc(const raya_attn_desc* desc, const float* qkv, float* ctx,
+                                                  const int32_t* valid_len, float rope_theta, void* stream);
+
 /* Stage timing, the counterpart of Tiled::attend_with_stages / StageTimes
  * (tiled/mod.rs:60-126, tiled/stages.rs:1-31): raya_attn_forward_ex with a
  * tiled kernel (kernel_id AUTO, TILED64 or a TILED64_* variant) whose warps

@@ -24,6 +24,7 @@ EXPORTS = (
     "raya_attn_work", "raya_attn_shard", "raya_attn_fill_normal",
     "raya_attn_ffma_peak", "raya_attn_version", "raya_attn_forward_timed",
     "raya_attn_probe_timeout", "raya_attn_forward_packed", "raya_attn_packed_workspace",
+    "raya_attn_forward_packed_noalloc",
 )
 
 
@@ -68,6 +69,8 @@ def _load() -> ctypes.CDLL:
     lib.raya_attn_forward_packed.restype = st
     lib.raya_attn_packed_workspace.argtypes = [dp, ctypes.c_float, ctypes.POINTER(ctypes.c_size_t)]
     lib.raya_attn_packed_workspace.restype = st
+    lib.raya_attn_forward_packed_noalloc.argtypes = [dp, vp, vp, vp, ctypes.c_float, vp]
+    lib.raya_attn_forward_packed_noalloc.restype = st
     lib.raya_attn_probe_timeout.argtypes = [ctypes.c_int64, vp]
     lib.raya_attn_probe_timeout.restype = st
     lib.raya_attn_sync_status.argtypes = [vp]

@@ -425,6 +425,38 @@ __global__ void timeout_probe_kernel(int* status, long long timeout_cycles) {
   mbar_wait_bounded(&bar, 0, &abort_flag, status, timeout_cycles);
 }
 
+// ---- Allocation-free rotary table ----
+// Some callers cannot allocate device memory for the rotary table that
+// raya_attn_forward_packed takes as a workspace: a serving runtime that owns
+// all of the GPU's memory through its own pool, a binding that only receives
+// raw device pointers from its host and holds no allocator, or a
+// latency-bound loop in which cudaMalloc (which may synchronise the device)
+// must not run.  raya_attn_forward_packed_noalloc keeps the table in this
+// file-scope array instead: kStaticRopeMaxSeq positions x 32 (cos, sin)
+// pairs = 2 MiB, held by every GPU that loads the library until the process
+// exits.
+constexpr int kStaticRopeMaxSeq = 8192;
+static __device__ __align__(256) float2 g_rope_static[kStaticRopeMaxSeq * 32];
+
+// The array's device address on each device, looked up once per device with
+// that device current (host code cannot use the symbol itself: in host code
+// it names a host-side stand-in, not device memory).
+std::mutex g_rope_static_mu;
+float2* g_rope_static_ptr[kMaxDevices] = {};
+
+raya_attn_status rope_static_table(int dev, float2** out) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(RAYA_ATTN_ERR_CUDA, "cuda: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_rope_static_mu);
+  if (!g_rope_static_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_rope_static);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(rotary table)");
+    g_rope_static_ptr[dev] = static_cast<float2*>(p);
+  }
+  *out = g_rope_static_ptr[dev];
+  return RAYA_ATTN_OK;
+}
+
 }  // namespace
 }  // namespace raya
 
@@ -527,6 +559,72 @@ raya_attn_status raya_attn_forward_packed(const raya_attn_desc* desc, const floa
   const int bm = pv->warps * pv->rows_per_warp;
   AttnArgs a = make_args(desc, qkv, qkv, qkv, ctx, valid_len, ctx_dev->status);
   a.rope_cs = rope ? static_cast<const float*>(workspace) : nullptr;
+  a.row_tiles = static_cast<int>((desc->seq + bm - 1) / bm);
+  const long long grid = static_cast<long long>(desc->batch) * desc->heads * a.row_tiles;
+  if (grid > 0x7fffffffll)
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
+  tiled64::TmaMaps maps;
+  const uint64_t rows = static_cast<uint64_t>(desc->batch) * desc->seq;
+  st = encode_packed(&maps.q, qkv, rows, desc->heads, static_cast<uint32_t>(bm));
+  if (st == RAYA_ATTN_OK) st = encode_packed(&maps.k, qkv, rows, desc->heads, tiled64::kBN);
+  if (st != RAYA_ATTN_OK) return st;
+  maps.v = maps.k;
+  (rope ? pv->rope : pv->plain)<<<static_cast<unsigned>(grid), pv->warps * 32, pv->smem, s>>>(a, maps);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "packed kernel launch");
+  return RAYA_ATTN_OK;
+}
+
+raya_attn_status raya_attn_forward_packed_noalloc(const raya_attn_desc* desc, const float* qkv, float* ctx,
+                                                  const int32_t* valid_len, float rope_theta, void* stream) {
+  raya_attn_status st = check_shape(desc);
+  if (st != RAYA_ATTN_OK) return st;
+  if (desc->head_dim != 64)
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the packed layout needs head_dim 64, got %lld",
+                static_cast<long long>(desc->head_dim));
+  if (!std::isfinite(rope_theta) || rope_theta < 0.f)
+    return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: rope_theta %g", static_cast<double>(rope_theta));
+  const bool rope = rope_theta > 0.f;
+  if (rope && desc->seq > kStaticRopeMaxSeq)
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED,
+                "unsupported: seq %lld exceeds the %d positions of the built-in rotary table "
+                "(use raya_attn_forward_packed with a workspace)",
+                static_cast<long long>(desc->seq), kStaticRopeMaxSeq);
+  if (desc->seq == 0) return RAYA_ATTN_OK;
+  if (!qkv || !ctx) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null tensor pointer");
+  if (!aligned16(qkv) || !aligned16(ctx))
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: tensors must be 16-byte aligned");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DeviceCtx* ctx_dev = nullptr;
+  st = ensure_ready(dev, &ctx_dev);
+  if (st != RAYA_ATTN_OK) return st;
+  float2* table = nullptr;
+  if (rope) {
+    st = rope_static_table(dev, &table);
+    if (st != RAYA_ATTN_OK) return st;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (rope) {
+    // Rewrites positions [0, seq) of the shared table; the attention kernel
+    // below reads only those (rows past valid_len <= seq are not rotated), so
+    // nothing left by an earlier call is read and nothing needs clearing.
+    RopeFreq f;
+    for (int i = 0; i < 32; ++i)  // ops.rs:120-122, in f32 with the C library's powf
+      f.inv_freq[i] = 1.0f / powf(rope_theta, static_cast<float>(2 * i) / 64.0f);
+    const int n = static_cast<int>(desc->seq) * 32;
+    rope_table_kernel<<<(n + 255) / 256, 256, 0, s>>>(table, static_cast<int>(desc->seq), f);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "rope table launch");
+  }
+  const int id = tuned_tiled(desc);
+  const PackedVariant* pv = nullptr;
+  for (const PackedVariant& v : kPacked)
+    if (v.id == id) pv = &v;
+  const int bm = pv->warps * pv->rows_per_warp;
+  AttnArgs a = make_args(desc, qkv, qkv, qkv, ctx, valid_len, ctx_dev->status);
+  a.rope_cs = rope ? reinterpret_cast<const float*>(table) : nullptr;
   a.row_tiles = static_cast<int>((desc->seq + bm - 1) / bm);
   const long long grid = static_cast<long long>(desc->batch) * desc->heads * a.row_tiles;
   if (grid > 0x7fffffffll)
