@@ -43,7 +43,7 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", default="c2")
     ap.add_argument("--halo", type=int, default=1)
-    ap.add_argument("--kernel", type=int, default=0, help="0 auto, 1 tiled64, 2 rowwise")
+    ap.add_argument("--kernel", type=int, default=0, help="0 auto, 1 tiled64, 2 rowwise, 32 tc32 (3xTF32 tensor cores)")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -367,7 +367,7 @@ def run_b200(args) -> None:
     # Stage proportions of one extra, instrumented launch (the reference
     # bench's "stages" field, benches/local_attention.rs:127-130,155-157).
     stages = None
-    if args.kernel != 2 and not args.packed:
+    if args.kernel not in (rb.KERNEL_ROWWISE, rb.KERNEL_TC32) and not args.packed:
         st = rb.stage_times(shape, params, q, k, v, out, valid_len=dvalid,
                             kernel=args.kernel or rb.KERNEL_TILED64)
         stages = {key: round(val, 2) for key, val in st.items() if key.endswith("pct")}
@@ -392,7 +392,8 @@ def run_b200(args) -> None:
         "gpu_launches": args.steps * w.layers,
         "layout": ("packed qkv -> context" + (f", rope theta {args.rope_theta:g}" if args.rope_theta else "")
                    if args.packed else "head-major q, k, v -> out"),
-        "kernel": "rowwise (raya_b200/csrc/rowwise.cuh)" if args.kernel == 2 else
+        "kernel": "rowwise (raya_b200/csrc/rowwise.cuh)" if args.kernel == rb.KERNEL_ROWWISE else
+                  "tc32, 3xTF32 tcgen05 (raya_b200/csrc/tc32.cuh)" if args.kernel == rb.KERNEL_TC32 else
                   f"tiled64 (raya_b200/csrc/tiled64.cuh), kernel id {args.kernel or 1}",
         "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "stages": stages,
     }

@@ -84,7 +84,10 @@ typedef enum {
   RAYA_KERNEL_TILED64_W4R32 = 16,
   RAYA_KERNEL_TILED64_W4R16 = 19,
   RAYA_KERNEL_TILED64_W4R16_P2 = 20,
-  RAYA_KERNEL_TILED64_W4R32_P2 = 21
+  RAYA_KERNEL_TILED64_W4R32_P2 = 21,
+  /* Tensor cores (tcgen05, kind::tf32) in 3xTF32: hi/lo split operands,
+   * fp32-level accuracy; head_dim 64, 128-row CTAs. */
+  RAYA_KERNEL_TC32 = 32
 } raya_kernel_id;
 
 /* Argument checks of validate (attention.rs:128-170), extended to the batch

@@ -19,6 +19,7 @@
 #include "../../include/raya_attn.h"
 #include "common.cuh"
 #include "rowwise.cuh"
+#include "tc32.cuh"
 #include "tiled64.cuh"
 
 namespace raya {
@@ -140,6 +141,9 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tiled64 smem)");
       }
     }
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_fwd),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::smem_bytes()));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32 smem)");
     for (const PackedVariant& pv : kPacked) {
       for (auto fn : {pv.plain, pv.rope}) {
         e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
@@ -153,8 +157,7 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
   return RAYA_ATTN_OK;
 }
 
-// A 2-D tensor map over a [rows][64] fp32 tensor with boxes of
-// [box_rows][32 floats], 128-byte swizzle, zero fill out of bounds.
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 raya_attn_status load_encoder() {
   std::call_once(g_encode_once, [] {
     cudaDriverEntryPointQueryResult q;
@@ -167,7 +170,11 @@ raya_attn_status load_encoder() {
   return RAYA_ATTN_OK;
 }
 
-raya_attn_status encode_rows64(CUtensorMap* map, const float* base, uint64_t rows, uint32_t box_rows) {
+// A 2-D tensor map over a [rows][64] fp32 tensor with boxes of
+// [box_rows][32 floats], zero fill out of bounds; 128-byte swizzle of
+// 16-byte chunks unless another swizzle is asked for.
+raya_attn_status encode_rows64(CUtensorMap* map, const float* base, uint64_t rows, uint32_t box_rows,
+                               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   raya_attn_status st = load_encoder();
   if (st != RAYA_ATTN_OK) return st;
   const cuuint64_t gdim[2] = {64, rows};
@@ -176,7 +183,7 @@ raya_attn_status encode_rows64(CUtensorMap* map, const float* base, uint64_t row
   const cuuint32_t estride[2] = {1, 1};
   const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim,
                               gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(RAYA_ATTN_ERR_CUDA, "cuda: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return RAYA_ATTN_OK;
@@ -315,6 +322,21 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     if (st != RAYA_ATTN_OK) return st;
     auto fn = stage_cycles ? tv->timed : tv->fn;
     fn<<<static_cast<unsigned>(grid), tv->warps * 32, tv->smem, stream>>>(a, maps);
+  } else if (kernel_id == RAYA_KERNEL_TC32 && !stage_cycles) {
+    if (d->head_dim != 64)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tensor-core kernel needs head_dim 64, got %lld",
+                  static_cast<long long>(d->head_dim));
+    a.row_tiles = static_cast<int>((d->seq + tc32::kBM - 1) / tc32::kBM);
+    const long long grid = static_cast<long long>(d->batch) * d->heads * a.row_tiles;
+    if (grid > 0x7fffffffll)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
+    tiled64::TmaMaps maps;
+    const uint64_t rows = static_cast<uint64_t>(d->batch) * d->heads * d->seq;
+    raya_attn_status st = encode_rows64(&maps.q, q, rows, tc32::kBM);
+    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.k, k, rows, tc32::kBN);
+    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tc32::kBN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    if (st != RAYA_ATTN_OK) return st;
+    tc32::tc32_fwd<<<static_cast<unsigned>(grid), tc32::kThreads, tc32::smem_bytes(), stream>>>(a, maps);
   } else if (stage_cycles) {
     return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: stage timing needs a tiled kernel");
   } else if (kernel_id == RAYA_KERNEL_ROWWISE) {

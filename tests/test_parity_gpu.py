@@ -18,9 +18,11 @@ from _util import (assert_close, cuda_device_run, cuda_host_run, load_golden,
 
 pytestmark = pytest.mark.gpu
 
-KERNELS_D64 = [rb.KERNEL_TILED64, rb.KERNEL_ROWWISE]
+KERNELS_D64 = [rb.KERNEL_TILED64, rb.KERNEL_ROWWISE, rb.KERNEL_TC32]
 # every compiled variant of the tiled kernel (warps per CTA x K/V stages)
 TILED_VARIANTS = [rb.KERNEL_TILED64] + sorted(rb._lib.KERNEL_TILED64_VARIANTS.values())
+# every head_dim-64 kernel: the FFMA variants, rowwise, and the 3xTF32 tensor-core kernel
+ALL_D64 = TILED_VARIANTS + [rb.KERNEL_ROWWISE, rb.KERNEL_TC32]
 B3 = dict(mask=oracle.MASK_BLOCK, block=128, halo=1)
 W64 = dict(mask=oracle.MASK_WINDOW, window=64)
 
@@ -53,7 +55,7 @@ def test_block_local_golden_host_call(cuda_device):
 
 @pytest.mark.parametrize("mask", [B3, W64], ids=["block3", "window64"])
 @pytest.mark.parametrize("seq", [1, 127, 128, 129, 1000, 2048])
-@pytest.mark.parametrize("kernel", TILED_VARIANTS + [rb.KERNEL_ROWWISE])
+@pytest.mark.parametrize("kernel", ALL_D64)
 def test_matches_oracle_at_edge_lengths(cuda_device, mask, seq, kernel):
     """equivalence.rs:29-42."""
     heads = 2 if seq >= 1000 else 3
@@ -94,7 +96,7 @@ def test_masks_are_exact(cuda_device, mask, d):
     p = oracle.Problem(1, 1, n, d, **mask)
     q, k = oracle.rand_vec(p.numel, 5), oracle.rand_vec(p.numel, 6)
     m = rb.Mask.BLOCK3 if mask is B3 else rb.Mask.WINDOW64
-    kernels = [rb.KERNEL_AUTO] + ([rb.KERNEL_ROWWISE] if d == 64 else [])
+    kernels = [rb.KERNEL_AUTO] + ([rb.KERNEL_ROWWISE, rb.KERNEL_TC32] if d == 64 else [])
     for kernel in kernels:
         for j in [0, 1, 63, 64, 65, 127, 128, 129, 191, 255, 256, 299]:
             v = np.zeros(p.numel, dtype=np.float32)
@@ -160,7 +162,7 @@ def test_nothing_valid_gives_all_zero_rows(cuda_device):
 
 @pytest.mark.parametrize("block", [32, 64, 128, 256, 48, 7, 1])
 @pytest.mark.parametrize("halo", [0, 1, 2])
-@pytest.mark.parametrize("kernel", TILED_VARIANTS + [rb.KERNEL_ROWWISE])
+@pytest.mark.parametrize("kernel", ALL_D64)
 def test_block_sizes_halos_and_ragged_batches(cuda_device, block, halo, kernel):
     """Extensions: any block size, halo, batch > 1 with per-sequence valid_len."""
     p = oracle.Problem(3, 2, 700, 64, mask=oracle.MASK_BLOCK, block=block, halo=halo)
@@ -172,7 +174,7 @@ def test_block_sizes_halos_and_ragged_batches(cuda_device, block, halo, kernel):
 
 
 @pytest.mark.parametrize("window", [0, 1, 31, 64, 100, 500])
-@pytest.mark.parametrize("kernel", TILED_VARIANTS + [rb.KERNEL_ROWWISE])
+@pytest.mark.parametrize("kernel", ALL_D64)
 def test_windows_and_ragged_batches(cuda_device, window, kernel):
     p = oracle.Problem(2, 2, 520, 64, mask=oracle.MASK_WINDOW, window=window)
     q, k, v = oracle.qkv(p.numel, 2000 + window)
@@ -211,7 +213,7 @@ def test_results_are_bitwise_reproducible_and_shard_invariant(cuda_device):
 
 @pytest.mark.parametrize("mask", [dict(mask=oracle.MASK_BLOCK, block=64, halo=1), W64,
                                   dict(mask=oracle.MASK_FULL)], ids=["block64", "window64", "full"])
-@pytest.mark.parametrize("kernel", TILED_VARIANTS + [rb.KERNEL_ROWWISE])
+@pytest.mark.parametrize("kernel", ALL_D64)
 def test_padding_values_never_reach_the_output(cuda_device, mask, kernel):
     """Rows at or past valid_len are padding: the reference never reads them
     (naive.rs:37, tile.rs:80-87).  Filled with NaN and Inf here, they must not
