@@ -134,11 +134,17 @@ class ClockSampler:
                 "window": "1 s soak of the same step + the timed region, 50 ms period"}
 
 
-def load_peaks() -> dict:
+# Used only when MEASURED_PEAKS.json is absent: an earlier measurement of
+# this pool's B200s (STREAM-style copy; cuBLAS bf16 GEMM burst).
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    """(peaks, "measured" | "fallback")."""
     try:
-        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))), "measured"
     except (OSError, ValueError):
-        return {}
+        return dict(FALLBACK_PEAKS), "fallback"
 
 
 def load_traffic(key: str):
@@ -253,6 +259,9 @@ def run_b200(args) -> None:
     pairs, rows = pairs * w.layers, rows * w.layers
     dvalid = torch.from_numpy(valid).to(dev)
     kern = rb.Cuda(rb.CudaConfig(device=local, kernel=args.kernel))
+    # the kernel that runs: the automatic choice, or the one asked for
+    chosen = rb.kernel_for(shape, params, packed=args.packed) if args.kernel == rb.KERNEL_AUTO else args.kernel
+    tiled_ids = set(rb._lib.KERNEL_TILED64_VARIANTS.values()) | {rb.KERNEL_TILED64}
     stream = torch.cuda.current_stream(dev)
 
     # Live FFMA peak of this GPU (the roofline denominator: no FP32 figure is
@@ -323,18 +332,32 @@ def run_b200(args) -> None:
     bytes_launch = 4.0 * D * (3 * float(valid.sum()) + w.batch * w.seq) * w.heads
     launch_ms = ms / w.layers
     achieved_tf = flops_launch / (launch_ms * 1e-3) / 1e12
-    peaks = load_peaks()
+    peaks, peak_kind = load_peaks()
     hbm = peaks.get("hbm_gbs")
-    tkey = f"{w.name}-halo{w.halo}"
-    roofline = {"bound": "ffma", "achieved": round(achieved_tf, 3), "peak": round(ffma_tflops, 3),
-                "unit": "TFLOP/s", "frac": round(achieved_tf / ffma_tflops, 4),
-                "peak_source": "measured live: raya_attn_ffma_peak (FP32 FFMA probe, this GPU)",
-                "nominal_peak": round(148 * 128 * 2 * 1.965e9 / 1e12, 1),
-                "traffic": load_traffic(tkey),
-                "algorithmic_bytes": bytes_launch,
-                "hbm": {"achieved": round(bytes_launch / (launch_ms * 1e-3) / 1e9, 1), "peak": hbm,
-                        "unit": "GB/s", "frac": round(bytes_launch / (launch_ms * 1e-3) / 1e9 / hbm, 4) if hbm else None,
-                        "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if hbm else None}}
+    tkey = f"{w.name}-halo{w.halo}" + ("-tc32" if chosen == rb.KERNEL_TC32 else "")
+    hbm_obj = {"achieved": round(bytes_launch / (launch_ms * 1e-3) / 1e9, 1), "peak": hbm,
+               "unit": "GB/s", "frac": round(bytes_launch / (launch_ms * 1e-3) / 1e9 / hbm, 4) if hbm else None,
+               "peak_source": f"MEASURED_PEAKS.json hbm_gbs (of {peak_kind})" if peak_kind == "measured"
+               else "fallback copy bandwidth of this pool (of fallback)"}
+    if chosen == rb.KERNEL_TC32:
+        # 3xTF32 issues three TF32 products per fp32 product: the algorithmic
+        # tensor work is 3 x 4 * head_dim per allowed pair.  Dense TF32 runs at
+        # half the bf16 rate.
+        tf32_peak = peaks["bf16_tflops"] / 2
+        roofline = {"bound": "tensor", "achieved": round(3 * achieved_tf, 3), "peak": round(tf32_peak, 1),
+                    "unit": "TFLOP/s", "frac": round(3 * achieved_tf / tf32_peak, 4),
+                    "peak_source": f"dense TF32 = bf16_tflops / 2 (of {peak_kind})",
+                    "work": "3 TF32 products (hi*lo, lo*hi, hi*hi) x 4 * head_dim flops per allowed pair",
+                    "fp32_equivalent": {"achieved": round(achieved_tf, 3), "ffma_peak": round(ffma_tflops, 3),
+                                        "frac": round(achieved_tf / ffma_tflops, 4)},
+                    "traffic": load_traffic(tkey), "algorithmic_bytes": bytes_launch, "hbm": hbm_obj}
+    else:
+        roofline = {"bound": "ffma", "achieved": round(achieved_tf, 3), "peak": round(ffma_tflops, 3),
+                    "unit": "TFLOP/s", "frac": round(achieved_tf / ffma_tflops, 4),
+                    "peak_source": "measured live: raya_attn_ffma_peak (FP32 FFMA probe, this GPU)",
+                    "nominal_peak": round(148 * 128 * 2 * 1.965e9 / 1e12, 1),
+                    "traffic": load_traffic(tkey),
+                    "algorithmic_bytes": bytes_launch, "hbm": hbm_obj}
 
     # End to end through the host-buffer API (pinned inputs, synchronous).
     e2e = None
@@ -361,15 +384,14 @@ def run_b200(args) -> None:
         # the host call must agree with the device call (bit for bit when both
         # run the same kernel; --kernel may pick another variant for the device)
         diff = float((ho - out.cpu()).abs().max())
-        assert diff < 1e-5 and (args.kernel not in (0, 1) or diff == 0.0), \
+        assert diff < 1e-5 and (args.kernel != 0 or diff == 0.0), \
             f"host-buffer call differs from the device call by {diff}"
 
     # Stage proportions of one extra, instrumented launch (the reference
     # bench's "stages" field, benches/local_attention.rs:127-130,155-157).
     stages = None
-    if args.kernel not in (rb.KERNEL_ROWWISE, rb.KERNEL_TC32) and not args.packed:
-        st = rb.stage_times(shape, params, q, k, v, out, valid_len=dvalid,
-                            kernel=args.kernel or rb.KERNEL_TILED64)
+    if chosen in tiled_ids and not args.packed:
+        st = rb.stage_times(shape, params, q, k, v, out, valid_len=dvalid, kernel=chosen)
         stages = {key: round(val, 2) for key, val in st.items() if key.endswith("pct")}
 
     cpu = None
@@ -388,13 +410,14 @@ def run_b200(args) -> None:
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), device-generated)",
         "config": workload_config(w, world),
         "queries_per_s": round(qps, 1),
-        "frac_fp32_peak": roofline["frac"],
+        "frac_fp32_peak": round(achieved_tf / ffma_tflops, 4),
         "gpu_launches": args.steps * w.layers,
         "layout": ("packed qkv -> context" + (f", rope theta {args.rope_theta:g}" if args.rope_theta else "")
                    if args.packed else "head-major q, k, v -> out"),
-        "kernel": "rowwise (raya_b200/csrc/rowwise.cuh)" if args.kernel == rb.KERNEL_ROWWISE else
-                  "tc32, 3xTF32 tcgen05 (raya_b200/csrc/tc32.cuh)" if args.kernel == rb.KERNEL_TC32 else
-                  f"tiled64 (raya_b200/csrc/tiled64.cuh), kernel id {args.kernel or 1}",
+        "kernel": "rowwise (raya_b200/csrc/rowwise.cuh)" if chosen == rb.KERNEL_ROWWISE else
+                  "tc32, 3xTF32 tcgen05 (raya_b200/csrc/tc32.cuh), kernel id 32" if chosen == rb.KERNEL_TC32 else
+                  f"tiled64 (raya_b200/csrc/tiled64.cuh), kernel id {chosen}",
+        "kernel_choice": "automatic (raya_attn_kernel_for)" if args.kernel == rb.KERNEL_AUTO else "--kernel",
         "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "stages": stages,
     }
     print(json.dumps(line), flush=True)

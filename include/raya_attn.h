@@ -73,7 +73,10 @@ typedef struct {
 
 /* Kernel selection for raya_attn_forward_ex (tests and benchmarks). */
 typedef enum {
-  RAYA_KERNEL_AUTO = 0,     /* tiled kernel when head_dim == 64, else rowwise */
+  RAYA_KERNEL_AUTO = 0,     /* head_dim 64: the tensor-core kernel for Full, windows of
+                               half width >= 64 and block masks whose allowed keys fill
+                               >= 80% of a 128-row CTA's key span, else the tuned tiled
+                               kernel; other head_dims: rowwise */
   RAYA_KERNEL_TILED64 = 1,  /* the tuned tiled variant for the mask and block (head_dim 64):
                                W4R16_P2 for block <= 64 and windows, W4R32_P2 for
                                block >= 128 and Full */
@@ -196,6 +199,14 @@ raya_attn_status raya_attn_probe_timeout(int64_t timeout_cycles, void* stream);
 /* Message of the last error raised on the calling thread (KernelError's
  * Display text for the reference's errors).  Never NULL. */
 const char* raya_attn_last_error(void);
+
+/* The kernel that raya_attn_forward, raya_attn_forward_host and
+ * raya_attn_forward_ex(RAYA_KERNEL_AUTO) launch for this descriptor, or with
+ * packed != 0 the packed entry points (a raya_kernel_id, the tiled kernel
+ * resolved to its tuned variant).  Host-only: no device work.  No counterpart
+ * in the reference, whose caller picks the kernel type itself
+ * (crates/raya-kernels/src/attention.rs:113-125). */
+raya_attn_status raya_attn_kernel_for(const raya_attn_desc* desc, int packed, int* kernel);
 
 /* Exact algorithmic work of one call: allowed (query < valid, key < valid,
  * mask-allowed) pairs and valid query rows, summed over batch and heads.

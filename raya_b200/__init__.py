@@ -7,13 +7,13 @@ this package is its host-side mirror of the reference interface.
 """
 from .attention import (BLOCK, WINDOW, AttentionKernel, AttnParams, AttnShape, Cuda, CudaConfig,
                         CudaError, DeviceTimeout, KernelError, LengthError, Mask, ShapeError,
-                        UnsupportedError, fill_normal, ffma_peak, make_desc, shard, stage_times,
-                        sync_status, validate, work)
+                        UnsupportedError, fill_normal, ffma_peak, kernel_for, make_desc, shard,
+                        stage_times, sync_status, validate, work)
 from ._lib import KERNEL_AUTO, KERNEL_ROWWISE, KERNEL_TC32, KERNEL_TILED64, LIB_PATH
 
 __all__ = [
     "BLOCK", "WINDOW", "AttentionKernel", "AttnParams", "AttnShape", "Cuda", "CudaConfig",
     "CudaError", "DeviceTimeout", "KernelError", "LengthError", "Mask", "ShapeError",
-    "UnsupportedError", "fill_normal", "ffma_peak", "make_desc", "shard", "stage_times", "sync_status",
+    "UnsupportedError", "fill_normal", "ffma_peak", "kernel_for", "make_desc", "shard", "stage_times", "sync_status",
     "validate", "work", "KERNEL_AUTO", "KERNEL_ROWWISE", "KERNEL_TC32", "KERNEL_TILED64", "LIB_PATH",
 ]

@@ -25,7 +25,7 @@ EXPORTS = (
     "raya_attn_work", "raya_attn_shard", "raya_attn_fill_normal",
     "raya_attn_ffma_peak", "raya_attn_version", "raya_attn_forward_timed",
     "raya_attn_probe_timeout", "raya_attn_forward_packed", "raya_attn_packed_workspace",
-    "raya_attn_forward_packed_noalloc",
+    "raya_attn_forward_packed_noalloc", "raya_attn_kernel_for",
 )
 
 
@@ -88,6 +88,8 @@ def _load() -> ctypes.CDLL:
     lib.raya_attn_fill_normal.restype = st
     lib.raya_attn_ffma_peak.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
     lib.raya_attn_ffma_peak.restype = st
+    lib.raya_attn_kernel_for.argtypes = [dp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+    lib.raya_attn_kernel_for.restype = st
     lib.raya_attn_version.argtypes = []
     lib.raya_attn_version.restype = ctypes.c_int
     return lib

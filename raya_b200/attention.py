@@ -224,6 +224,15 @@ def work(shape: AttnShape, params: AttnParams) -> tuple[int, int]:
     return pairs.value, rows.value
 
 
+def kernel_for(shape: AttnShape, params: AttnParams, packed: bool = False) -> int:
+    """The kernel id the automatic choice launches for this call, in the
+    head-major or (``packed``) the caller's packed layout (host-only)."""
+    d = make_desc(shape, params)
+    kid = ctypes.c_int()
+    _check(lib.raya_attn_kernel_for(ctypes.byref(d), int(packed), ctypes.byref(kid)))
+    return kid.value
+
+
 def shard(shape: AttnShape, params: AttnParams, world: int, rank: int) -> tuple[int, int]:
     """[begin, end) of flattened batch*heads slices owned by ``rank``."""
     valid = params.valid_array(shape.batch)

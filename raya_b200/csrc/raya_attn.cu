@@ -83,6 +83,24 @@ int tuned_tiled(const raya_attn_desc* d) {
   return long_span ? RAYA_KERNEL_TILED64_W4R32_P2 : RAYA_KERNEL_TILED64_W4R16_P2;
 }
 
+// The automatic choice for head_dim 64.  The tensor-core kernel computes all
+// keys of a 128-row CTA's key span for every row of the CTA, so it wins where
+// most of that span is allowed for most rows (measured on B200 over block
+// 32..256, halo 0..2, Window64 and Full): Full, windows of half width >= 64,
+// and block masks whose allowed keys per row, (2*halo + 1) * block, are at
+// least 80% of the span; otherwise the tuned FFMA kernel.
+int auto_kernel(const raya_attn_desc* d) {
+  if (d->head_dim != 64) return RAYA_KERNEL_ROWWISE;
+  if (d->mask == RAYA_MASK_FULL) return RAYA_KERNEL_TC32;
+  if (d->mask == RAYA_MASK_WINDOW) return d->window >= 64 ? RAYA_KERNEL_TC32 : tuned_tiled(d);
+  const long long blk = d->block, halo = d->halo;
+  if (blk >= tc32::kBM) return RAYA_KERNEL_TC32;
+  const long long spanned = (tc32::kBM + blk - 1) / blk + (tc32::kBM % blk != 0 ? 1 : 0);
+  const long long span = ((spanned + 2 * halo) * blk + tc32::kBN - 1) / tc32::kBN * tc32::kBN;
+  const long long allowed = (2 * halo + 1) * blk;
+  return 5 * allowed >= 4 * span ? RAYA_KERNEL_TC32 : tuned_tiled(d);
+}
+
 // Device status word: bit 0 = a bounded wait gave up.  One per device that
 // loads the library; its device address is looked up once per device.
 __device__ int g_status;
@@ -300,7 +318,7 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
   AttnArgs a = make_args(d, q, k, v, out, valid_len, ctx->status);
   a.stage_cycles = stage_cycles;
 
-  if (kernel_id == RAYA_KERNEL_AUTO) kernel_id = d->head_dim == 64 ? RAYA_KERNEL_TILED64 : RAYA_KERNEL_ROWWISE;
+  if (kernel_id == RAYA_KERNEL_AUTO) kernel_id = stage_cycles ? RAYA_KERNEL_TILED64 : auto_kernel(d);
   if (kernel_id == RAYA_KERNEL_TILED64) kernel_id = tuned_tiled(d);
   const TiledVariant* tv = nullptr;
   for (const TiledVariant& t : kTiled)
@@ -794,6 +812,15 @@ raya_attn_status raya_attn_forward_host(const raya_attn_desc* desc, const float*
     cudaMemcpy(ctx->status, &zero, sizeof zero, cudaMemcpyHostToDevice);
     return fail(RAYA_ATTN_ERR_TIMEOUT, "timeout: a device-side wait gave up (status 0x%x)", flag);
   }
+  return RAYA_ATTN_OK;
+}
+
+raya_attn_status raya_attn_kernel_for(const raya_attn_desc* desc, int packed, int* kernel) {
+  raya_attn_status st = check_shape(desc);
+  if (st != RAYA_ATTN_OK) return st;
+  if (!kernel) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null kernel pointer");
+  const int id = packed ? RAYA_KERNEL_TILED64 : auto_kernel(desc);
+  *kernel = id == RAYA_KERNEL_TILED64 ? tuned_tiled(desc) : id;
   return RAYA_ATTN_OK;
 }
 
