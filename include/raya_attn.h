@@ -90,7 +90,11 @@ typedef enum {
   RAYA_KERNEL_TILED64_W4R32_P2 = 21,
   /* Tensor cores (tcgen05, kind::tf32) in 3xTF32: hi/lo split operands,
    * fp32-level accuracy; head_dim 64, 128-row CTAs. */
-  RAYA_KERNEL_TC32 = 32
+  RAYA_KERNEL_TC32 = 32,
+  /* The same arithmetic, warp-specialised and pipelined: q and p held in
+   * tensor memory, a split warpgroup preparing K/V operand stages, one MMA
+   * thread overlapping QK^T of the next key tile with this tile's softmax. */
+  RAYA_KERNEL_TC32_PIPE = 33
 } raya_kernel_id;
 
 /* Argument checks of validate (attention.rs:128-170), extended to the batch

@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "rowwise.cuh"
 #include "tc32.cuh"
+#include "tc32_pipe.cuh"
 #include "tiled64.cuh"
 
 namespace raya {
@@ -162,6 +163,9 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
     e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_fwd),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::smem_bytes()));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32 smem)");
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_pipe_fwd),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::pipe_smem_bytes()));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_pipe smem)");
     for (const PackedVariant& pv : kPacked) {
       for (auto fn : {pv.plain, pv.rope}) {
         e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
@@ -355,6 +359,21 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tc32::kBN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     if (st != RAYA_ATTN_OK) return st;
     tc32::tc32_fwd<<<static_cast<unsigned>(grid), tc32::kThreads, tc32::smem_bytes(), stream>>>(a, maps);
+  } else if (kernel_id == RAYA_KERNEL_TC32_PIPE && !stage_cycles) {
+    if (d->head_dim != 64)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tensor-core kernel needs head_dim 64, got %lld",
+                  static_cast<long long>(d->head_dim));
+    a.row_tiles = static_cast<int>((d->seq + tc32::kBM - 1) / tc32::kBM);
+    const long long grid = static_cast<long long>(d->batch) * d->heads * a.row_tiles;
+    if (grid > 0x7fffffffll)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
+    tc32::PipeMaps maps;
+    const uint64_t rows = static_cast<uint64_t>(d->batch) * d->heads * d->seq;
+    raya_attn_status st = encode_rows64(&maps.k, k, rows, tc32::kBN);
+    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tc32::kBN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    if (st != RAYA_ATTN_OK) return st;
+    tc32::tc32_pipe_fwd<<<static_cast<unsigned>(grid), tc32::kPipeThreads, tc32::pipe_smem_bytes(), stream>>>(a,
+                                                                                                              maps);
   } else if (stage_cycles) {
     return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: stage timing needs a tiled kernel");
   } else if (kernel_id == RAYA_KERNEL_ROWWISE) {

@@ -119,6 +119,12 @@ __device__ __forceinline__ float tf32_rn(float x) {
   return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
+// x - trunc(x), where trunc(x) is the TF32 value the tensor core reads for
+// the fp32 bit pattern x (its 13 low mantissa bits dropped).  Exact in fp32.
+__device__ __forceinline__ float tf32_lo(float x) {
+  return __fsub_rn(x, __uint_as_float(__float_as_uint(x) & 0xFFFFE000u));
+}
+
 // Split pass over a [ROWS][64] swizzled tile: hi in place, lo into `lo`.
 // Rows at or past `nvalid` are zeroed in both (only asked for V).
 template <int ROWS>
