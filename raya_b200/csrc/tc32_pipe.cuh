@@ -22,9 +22,11 @@
 //              memory (the A operand of PV).
 //   warps 4-6  (split):   per key tile, waits for the raw K and V tiles (TMA
 //              into a ring of four stages; they are the hi operands), writes
-//              their lo parts (two stages), zeroes V rows at or past
-//              valid_len in both, and issues the TMA of the tile two ahead
-//              into the stage whose PV product has completed.
+//              their lo parts (a ring of three stages), zeroes V rows at or
+//              past valid_len in both, and issues the TMA of the next tile
+//              into the raw stage that PV(j-3) has released.  Three lo
+//              stages let the split of tile j+1 run while the tensor core
+//              works on QK(j) and PV(j-1).
 //   warp 7     (MMA):     one thread issues QK(j) into S[j%2], then PV(j-1)
 //              once P(j-1) is stored, so QK of the next tile runs while the
 //              softmax works on this one.
@@ -55,17 +57,19 @@ struct PipeMaps {
 };
 
 constexpr int kRawStages = 4;
+constexpr int kLoStages = 3;
 
 struct PipeSmem {
   float raw[kRawStages][2][2][kBN][32];  // [stage][K, V][column half][key][32]: TMA targets = hi operands
-  float lo[2][2][2][kBN][32];            // [stage][K lo, V lo][half][key][32]
-  uint64_t raw_full[kRawStages], kv_ready[2], kv_free[2], s_full[2], s_free[2];
+  float lo[kLoStages][2][2][kBN][32];    // [stage][K lo, V lo][half][key][32]
+  uint64_t raw_full[kRawStages], kv_ready[kLoStages], kv_free[kLoStages], s_full[2], s_free[2];
   uint64_t p_ready, pv_done, q_ready;
   uint32_t tmem_base;
   int abort_flag;
 };
 
 constexpr size_t pipe_smem_bytes() { return sizeof(PipeSmem) + 1024; }
+static_assert(pipe_smem_bytes() <= 232448, "more shared memory than one sm_100 block may hold");
 
 // D (+)= A B with A read from tensor memory (M = 128 rows in lanes, K = 8
 // 32-bit columns) and B from a shared-memory descriptor.
@@ -161,9 +165,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
   }
   if (tid == 0) {
     for (int s = 0; s < kRawStages; ++s) mbar_init(&sm.raw_full[s], 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kLoStages; ++s) {
       mbar_init(&sm.kv_ready[s], kSplitThreads);
       mbar_init(&sm.kv_free[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.s_full[s], 1);
       mbar_init(&sm.s_free[s], 128);
     }
@@ -324,24 +330,24 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
       tiled64::tma_load_2d(&sm.raw[s][1][1][0][0], &maps.v, 32, y, bar);
       last_tma_tile = jj;
     };
-    if (st == 0) {
-      issue(0);
-      if (ntiles > 1) issue(1);
-    }
+    if (st == 0)
+      for (int jj = 0; jj < kRawStages && jj < ntiles; ++jj) issue(jj);
     for (int j = 0; j < ntiles; ++j) {
-      const int s2 = j & 1, s4 = j & (kRawStages - 1);
+      const int s3 = j % kLoStages, s4 = j & (kRawStages - 1);
       bool w = true;
-      if (j >= 2)  // PV(j-2) is done: lo stage s2 and raw stage (j+2)%4 are free
-        w = mbar_wait_bounded(&sm.kv_free[s2], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag, a.status,
-                              a.timeout_cycles);
+      if (j >= kLoStages) {  // PV(j-3) is done: lo stage s3 and raw stage (j+1)%4 are free
+        w = mbar_wait_bounded(&sm.kv_free[s3], static_cast<uint32_t>(j / kLoStages - 1) & 1u, abort_flag,
+                              a.status, a.timeout_cycles);
+        if (w && st == 0 && j + 1 < ntiles) issue(j + 1);
+      }
       w = w && mbar_wait_bounded(&sm.raw_full[s4], static_cast<uint32_t>(j >> 2) & 1u, abort_flag, a.status,
                                  a.timeout_cycles);
       if (bar_any(kSplitBarrier, kSplitThreads, !w)) break;
       const int nv = min(kBN, valid - (t_begin + j) * kBN);
       float4* kr = reinterpret_cast<float4*>(&sm.raw[s4][0][0][0][0]);
       float4* vr = reinterpret_cast<float4*>(&sm.raw[s4][1][0][0][0]);
-      float4* kl = reinterpret_cast<float4*>(&sm.lo[s2][0][0][0][0]);
-      float4* vl = reinterpret_cast<float4*>(&sm.lo[s2][1][0][0][0]);
+      float4* kl = reinterpret_cast<float4*>(&sm.lo[s3][0][0][0][0]);
+      float4* vl = reinterpret_cast<float4*>(&sm.lo[s3][1][0][0][0]);
 #pragma unroll 4
       for (int f = st; f < kBN * 16; f += kSplitThreads) {
         const float4 x = kr[f];
@@ -366,9 +372,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
         }
       }
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
-      mbar_arrive(&sm.kv_ready[s2]);
+      mbar_arrive(&sm.kv_ready[s3]);
       bar_named(kSplitBarrier, kSplitThreads);
-      if (st == 0 && j + 2 < ntiles) issue(j + 2);
     }
   } else if ((tid & 31) == 0) {
     // ---------------- MMA issuer (one thread) ----------------
@@ -378,7 +383,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
       last_commit_parity = parity;
     };
     auto pv = [&](int jj) {
-      const int s = jj & 1;
+      const int s = jj % kLoStages;
       const uint32_t vh = smem_addr(&sm.raw[jj & (kRawStages - 1)][1][0][0][0]), vl = smem_addr(&sm.lo[s][1][0][0][0]);
       const uint32_t d = tmem + kColPV;
 #pragma unroll
@@ -388,20 +393,20 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
 #pragma unroll
       for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kColPh + 8 * k, v_desc(vh, k), kIdescPV, 1u);
       commit(&sm.pv_done, static_cast<uint32_t>(jj) & 1u);
-      if (jj + 2 < ntiles) commit(&sm.kv_free[s], static_cast<uint32_t>(jj >> 1) & 1u);
+      if (jj + kLoStages < ntiles) commit(&sm.kv_free[s], static_cast<uint32_t>(jj / kLoStages) & 1u);
     };
     bool ok = mbar_wait_bounded(&sm.q_ready, 0, abort_flag, a.status, a.timeout_cycles);
     int j = 0;
     for (; ok && j < ntiles; ++j) {
-      const int s = j & 1;
-      ok = mbar_wait_bounded(&sm.kv_ready[s], static_cast<uint32_t>(j >> 1) & 1u, abort_flag, a.status,
+      const int s = j & 1, s3 = j % kLoStages;
+      ok = mbar_wait_bounded(&sm.kv_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u, abort_flag, a.status,
                              a.timeout_cycles);
       if (ok && j >= 2)
         ok = mbar_wait_bounded(&sm.s_free[s], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag, a.status,
                                a.timeout_cycles);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t khi = smem_addr(&sm.raw[j & (kRawStages - 1)][0][0][0][0]), klo = smem_addr(&sm.lo[s][0][0][0][0]);
+      const uint32_t khi = smem_addr(&sm.raw[j & (kRawStages - 1)][0][0][0][0]), klo = smem_addr(&sm.lo[s3][0][0][0][0]);
       const uint32_t d = tmem + kColS + 64 * s;
 #pragma unroll
       for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kColQh + 8 * k, k_desc(klo, k), kIdescQK, k > 0 ? 1u : 0u);
