@@ -73,10 +73,11 @@ typedef struct {
 
 /* Kernel selection for raya_attn_forward_ex (tests and benchmarks). */
 typedef enum {
-  RAYA_KERNEL_AUTO = 0,     /* head_dim 64: the tensor-core kernel for Full, windows of
-                               half width >= 64 and block masks whose allowed keys fill
-                               >= 80% of a 128-row CTA's key span, else the tuned tiled
-                               kernel; other head_dims: rowwise */
+  RAYA_KERNEL_AUTO = 0,     /* head_dim 64: the pipelined tensor-core kernel for Full,
+                               windows of half width >= 64, blocks >= 128 and block masks
+                               with a halo whose allowed keys fill >= half of a 128-row
+                               CTA's key span, else the tuned tiled kernel; other
+                               head_dims: rowwise */
   RAYA_KERNEL_TILED64 = 1,  /* the tuned tiled variant for the mask and block (head_dim 64):
                                W4R16_P2 for block <= 64 and windows, W4R32_P2 for
                                block >= 128 and Full */

@@ -84,22 +84,24 @@ int tuned_tiled(const raya_attn_desc* d) {
   return long_span ? RAYA_KERNEL_TILED64_W4R32_P2 : RAYA_KERNEL_TILED64_W4R16_P2;
 }
 
-// The automatic choice for head_dim 64.  The tensor-core kernel computes all
-// keys of a 128-row CTA's key span for every row of the CTA, so it wins where
-// most of that span is allowed for most rows (measured on B200 over block
-// 32..256, halo 0..2, Window64 and Full): Full, windows of half width >= 64,
-// and block masks whose allowed keys per row, (2*halo + 1) * block, are at
-// least 80% of the span; otherwise the tuned FFMA kernel.
+// The automatic choice for head_dim 64 (measured on B200 over block 32..256,
+// halo 0..2, Window64 and Full).  The pipelined tensor-core kernel computes
+// every key of a 128-row CTA's key span for every row of the CTA; it wins
+// for Full, windows of half width >= 64, blocks >= 128, and block masks with
+// a halo whose allowed keys per row, (2*halo + 1) * block, are at least half
+// of that span.  With halo 0 and blocks below 128 the 64-row tiles of the
+// tuned FFMA kernel waste less and win.
 int auto_kernel(const raya_attn_desc* d) {
   if (d->head_dim != 64) return RAYA_KERNEL_ROWWISE;
-  if (d->mask == RAYA_MASK_FULL) return RAYA_KERNEL_TC32;
-  if (d->mask == RAYA_MASK_WINDOW) return d->window >= 64 ? RAYA_KERNEL_TC32 : tuned_tiled(d);
+  if (d->mask == RAYA_MASK_FULL) return RAYA_KERNEL_TC32_PIPE;
+  if (d->mask == RAYA_MASK_WINDOW) return d->window >= 64 ? RAYA_KERNEL_TC32_PIPE : tuned_tiled(d);
   const long long blk = d->block, halo = d->halo;
-  if (blk >= tc32::kBM) return RAYA_KERNEL_TC32;
+  if (blk >= tc32::kBM) return RAYA_KERNEL_TC32_PIPE;
+  if (halo == 0) return tuned_tiled(d);
   const long long spanned = (tc32::kBM + blk - 1) / blk + (tc32::kBM % blk != 0 ? 1 : 0);
   const long long span = ((spanned + 2 * halo) * blk + tc32::kBN - 1) / tc32::kBN * tc32::kBN;
   const long long allowed = (2 * halo + 1) * blk;
-  return 5 * allowed >= 4 * span ? RAYA_KERNEL_TC32 : tuned_tiled(d);
+  return 2 * allowed >= span ? RAYA_KERNEL_TC32_PIPE : tuned_tiled(d);
 }
 
 // Device status word: bit 0 = a bounded wait gave up.  One per device that

@@ -83,6 +83,10 @@ CONFIGS: dict[str, Workload] = {
     "c3-b256": Workload("c3-b256", 16, 12, 2048, 64, 256, 1, 2, 1.0, None),
     "c4": Workload("c4", 64, 12, 512, 64, 64, 1, 3, 0.5, (128, 512), layers=12),
     "c5": Workload("c5", 256, 16, 8192, 64, 128, 1, 4, 1.0, (4096, 8192)),
+    # c5's sequences at 1/32 of its batch (about 1 GB on the device): the
+    # size at which ncu captures the c5 kernel (its traffic scales by
+    # algorithmic bytes to the full c5 launch); not a benchmark line.
+    "c5-p": Workload("c5-p", 8, 16, 8192, 64, 128, 1, 4, 1.0, (4096, 8192)),
 }
 
 

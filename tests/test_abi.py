@@ -166,23 +166,24 @@ def test_packed_call_validates_on_the_host():
     (rb.Mask.block(1), 128, True),    # Block3: every allowed key of a 128-row span
     (rb.Mask.block(0), 256, True),
     (rb.Mask.block(2), 64, True),     # 320 of 384 span keys allowed per row
-    (rb.Mask.block(1), 64, False),    # 192 of 256
-    (rb.Mask.block(0), 64, False),
-    (rb.Mask.block(2), 32, False),
-    (rb.Mask.block(1), 7, False),
+    (rb.Mask.block(1), 64, True),     # 192 of 256
+    (rb.Mask.block(1), 32, True),     # 96 of 192
+    (rb.Mask.block(0), 64, False),    # halo 0 below 128: the 64-row FFMA tiles
+    (rb.Mask.block(2), 32, True),
+    (rb.Mask.block(1), 7, False),     # 21 of 192
     (rb.Mask.WINDOW64, 128, True),
     (rb.Mask.sliding(31), 128, False),
     (rb.Mask.FULL, 128, True),
 ])
 def test_automatic_kernel_choice(mask, block, expect_tc):
-    """The host-side rule behind RAYA_KERNEL_AUTO: the tensor-core kernel where
-    a 128-row CTA's key span is mostly allowed, the tuned FFMA kernel else,
-    rowwise for head_dim != 64 (no device work involved)."""
+    """The host-side rule behind RAYA_KERNEL_AUTO: the pipelined tensor-core
+    kernel where enough of a 128-row CTA's key span is allowed, the tuned FFMA
+    kernel else, rowwise for head_dim != 64 (no device work involved)."""
     shape = _shape(heads=2, seq=1024, d=64)
     params = rb.AttnParams.new(mask, 1024, 64, block=block)
     kid = rb.kernel_for(shape, params)
     if expect_tc:
-        assert kid == rb.KERNEL_TC32
+        assert kid == rb._lib.KERNEL_TC32_PIPE
     else:
         assert kid in _lib.KERNEL_TILED64_VARIANTS.values()
     assert rb.kernel_for(_shape(heads=2, seq=1024, d=32), rb.AttnParams.new(mask, 1024, 32, block=block)) \

@@ -54,7 +54,7 @@ def test_packed_layout_matches_split_rope_attend_merge(cuda_device, case, theta)
 
 def test_packed_layout_equals_the_head_major_call_bit_for_bit(cuda_device):
     """Without rotation the fused layout only changes addressing: the result is
-    the head-major call's, transposed, bit for bit."""
+    the head-major call's with the same kernel, transposed, bit for bit."""
     import torch
 
     batch, seq, heads = 2, 1000, 3
@@ -68,7 +68,7 @@ def test_packed_layout_equals_the_head_major_call_bit_for_bit(cuda_device):
     dev = torch.device("cuda", 0)
     tq, tk, tv = (torch.from_numpy(a).to(dev) for a in (q, k, v))
     out = torch.empty_like(tq)
-    rb.Cuda().attend_device(shape, params, tq, tk, tv, out)
+    rb.Cuda().attend_device(shape, params, tq, tk, tv, out, kernel=rb.kernel_for(shape, params, packed=True))
     rb.sync_status()
     head_major = out.cpu().numpy().reshape(batch, heads, seq, 64).transpose(0, 2, 1, 3).reshape(-1)
     assert np.array_equal(got, head_major)
