@@ -73,7 +73,7 @@ typedef struct {
 
 /* Kernel selection for raya_attn_forward_ex (tests and benchmarks). */
 typedef enum {
-  RAYA_KERNEL_AUTO = 0,     /* head_dim 64: the pipelined tensor-core kernel for Full,
+  RAYA_KERNEL_AUTO = 0,     /* head_dim 64: the tensor-core kernel RAYA_KERNEL_TC32_WS for Full,
                                windows of half width >= 64, blocks >= 128 and block masks
                                with a halo whose allowed keys fill >= half of a 128-row
                                CTA's key span, else the tuned tiled kernel; other
@@ -95,7 +95,12 @@ typedef enum {
   /* The same arithmetic, warp-specialised and pipelined: q and p held in
    * tensor memory, a split warpgroup preparing K/V operand stages, one MMA
    * thread overlapping QK^T of the next key tile with this tile's softmax. */
-  RAYA_KERNEL_TC32_PIPE = 33
+  RAYA_KERNEL_TC32_PIPE = 33,
+  /* The same, with QK^T and PV issued by two warps (one issuing thread
+   * sustains only ~2/3 of the tensor core's rate at N = 64) and the O
+   * accumulator in tensor memory, rescaled only when a row's max grows by
+   * more than 2^8. */
+  RAYA_KERNEL_TC32_WS = 34
 } raya_kernel_id;
 
 /* Argument checks of validate (attention.rs:128-170), extended to the batch

@@ -21,6 +21,7 @@
 #include "rowwise.cuh"
 #include "tc32.cuh"
 #include "tc32_pipe.cuh"
+#include "tc32_ws.cuh"
 #include "tiled64.cuh"
 
 namespace raya {
@@ -85,7 +86,7 @@ int tuned_tiled(const raya_attn_desc* d) {
 }
 
 // The automatic choice for head_dim 64 (measured on B200 over block 32..256,
-// halo 0..2, Window64 and Full).  The pipelined tensor-core kernel computes
+// halo 0..2, Window64 and Full).  The two-issuer tensor-core kernel computes
 // every key of a 128-row CTA's key span for every row of the CTA; it wins
 // for Full, windows of half width >= 64, blocks >= 128, and block masks with
 // a halo whose allowed keys per row, (2*halo + 1) * block, are at least half
@@ -93,15 +94,15 @@ int tuned_tiled(const raya_attn_desc* d) {
 // tuned FFMA kernel waste less and win.
 int auto_kernel(const raya_attn_desc* d) {
   if (d->head_dim != 64) return RAYA_KERNEL_ROWWISE;
-  if (d->mask == RAYA_MASK_FULL) return RAYA_KERNEL_TC32_PIPE;
-  if (d->mask == RAYA_MASK_WINDOW) return d->window >= 64 ? RAYA_KERNEL_TC32_PIPE : tuned_tiled(d);
+  if (d->mask == RAYA_MASK_FULL) return RAYA_KERNEL_TC32_WS;
+  if (d->mask == RAYA_MASK_WINDOW) return d->window >= 64 ? RAYA_KERNEL_TC32_WS : tuned_tiled(d);
   const long long blk = d->block, halo = d->halo;
-  if (blk >= tc32::kBM) return RAYA_KERNEL_TC32_PIPE;
+  if (blk >= tc32::kBM) return RAYA_KERNEL_TC32_WS;
   if (halo == 0) return tuned_tiled(d);
   const long long spanned = (tc32::kBM + blk - 1) / blk + (tc32::kBM % blk != 0 ? 1 : 0);
   const long long span = ((spanned + 2 * halo) * blk + tc32::kBN - 1) / tc32::kBN * tc32::kBN;
   const long long allowed = (2 * halo + 1) * blk;
-  return 2 * allowed >= span ? RAYA_KERNEL_TC32_PIPE : tuned_tiled(d);
+  return 2 * allowed >= span ? RAYA_KERNEL_TC32_WS : tuned_tiled(d);
 }
 
 // Device status word: bit 0 = a bounded wait gave up.  One per device that
@@ -168,6 +169,9 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
     e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_pipe_fwd),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::pipe_smem_bytes()));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_pipe smem)");
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_ws_fwd),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::pipe_smem_bytes()));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_ws smem)");
     for (const PackedVariant& pv : kPacked) {
       for (auto fn : {pv.plain, pv.rope}) {
         e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
@@ -361,7 +365,7 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tc32::kBN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     if (st != RAYA_ATTN_OK) return st;
     tc32::tc32_fwd<<<static_cast<unsigned>(grid), tc32::kThreads, tc32::smem_bytes(), stream>>>(a, maps);
-  } else if (kernel_id == RAYA_KERNEL_TC32_PIPE && !stage_cycles) {
+  } else if ((kernel_id == RAYA_KERNEL_TC32_PIPE || kernel_id == RAYA_KERNEL_TC32_WS) && !stage_cycles) {
     if (d->head_dim != 64)
       return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tensor-core kernel needs head_dim 64, got %lld",
                   static_cast<long long>(d->head_dim));
@@ -374,8 +378,11 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     raya_attn_status st = encode_rows64(&maps.k, k, rows, tc32::kBN);
     if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tc32::kBN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     if (st != RAYA_ATTN_OK) return st;
-    tc32::tc32_pipe_fwd<<<static_cast<unsigned>(grid), tc32::kPipeThreads, tc32::pipe_smem_bytes(), stream>>>(a,
-                                                                                                              maps);
+    if (kernel_id == RAYA_KERNEL_TC32_WS)
+      tc32::tc32_ws_fwd<<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
+    else
+      tc32::tc32_pipe_fwd<<<static_cast<unsigned>(grid), tc32::kPipeThreads, tc32::pipe_smem_bytes(), stream>>>(
+          a, maps);
   } else if (stage_cycles) {
     return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: stage timing needs a tiled kernel");
   } else if (kernel_id == RAYA_KERNEL_ROWWISE) {

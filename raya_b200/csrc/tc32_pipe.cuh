@@ -22,9 +22,11 @@
 //              memory (the A operand of PV).
 //   warps 4-6  (split):   per key tile, waits for the raw K and V tiles (TMA
 //              into a ring of four stages; they are the hi operands), writes
-//              their lo parts (a ring of three stages), zeroes V rows at or
-//              past valid_len in both, and issues the TMA of the next tile
-//              into the raw stage that PV(j-3) has released.  Three lo
+//              their lo parts (a ring of three stages; K's first, signalled on
+//              its own barrier so QK(j) can start while V's is written),
+//              zeroes V rows at or past valid_len in both, and issues the TMA
+//              of the next tile into the raw stage that PV(j-3) has released.
+//              Three lo
 //              stages let the split of tile j+1 run while the tensor core
 //              works on QK(j) and PV(j-1).
 //   warp 7     (MMA):     one thread issues QK(j) into S[j%2], then PV(j-1)
@@ -62,7 +64,7 @@ constexpr int kLoStages = 3;
 struct PipeSmem {
   float raw[kRawStages][2][2][kBN][32];  // [stage][K, V][column half][key][32]: TMA targets = hi operands
   float lo[kLoStages][2][2][kBN][32];    // [stage][K lo, V lo][half][key][32]
-  uint64_t raw_full[kRawStages], kv_ready[kLoStages], kv_free[kLoStages], s_full[2], s_free[2];
+  uint64_t raw_full[kRawStages], k_ready[kLoStages], v_ready[kLoStages], kv_free[kLoStages], s_full[2], s_free[2];
   uint64_t p_ready, pv_done, q_ready;
   uint32_t tmem_base;
   int abort_flag;
@@ -166,7 +168,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < kRawStages; ++s) mbar_init(&sm.raw_full[s], 1);
     for (int s = 0; s < kLoStages; ++s) {
-      mbar_init(&sm.kv_ready[s], kSplitThreads);
+      mbar_init(&sm.k_ready[s], kSplitThreads);
+      mbar_init(&sm.v_ready[s], kSplitThreads);
       mbar_init(&sm.kv_free[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -353,6 +356,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
         const float4 x = kr[f];
         kl[f] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
       }
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+      mbar_arrive(&sm.k_ready[s3]);  // QK(j) may start; V's lo part follows
       if (nv == kBN) {
 #pragma unroll 4
         for (int f = st; f < kBN * 16; f += kSplitThreads) {
@@ -371,8 +376,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
           }
         }
       }
-      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
-      mbar_arrive(&sm.kv_ready[s3]);
+      fence_proxy_async_smem();
+      mbar_arrive(&sm.v_ready[s3]);
       bar_named(kSplitBarrier, kSplitThreads);
     }
   } else if ((tid & 31) == 0) {
@@ -399,7 +404,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
     int j = 0;
     for (; ok && j < ntiles; ++j) {
       const int s = j & 1, s3 = j % kLoStages;
-      ok = mbar_wait_bounded(&sm.kv_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u, abort_flag, a.status,
+      ok = mbar_wait_bounded(&sm.k_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u, abort_flag, a.status,
                              a.timeout_cycles);
       if (ok && j >= 2)
         ok = mbar_wait_bounded(&sm.s_free[s], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag, a.status,
@@ -417,7 +422,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
       commit(&sm.s_full[s], static_cast<uint32_t>(j >> 1) & 1u);
       if (j >= 1) {
         ok = mbar_wait_bounded(&sm.p_ready, static_cast<uint32_t>(j - 1) & 1u, abort_flag, a.status,
-                               a.timeout_cycles);
+                               a.timeout_cycles) &&
+             mbar_wait_bounded(&sm.v_ready[(j - 1) % kLoStages], static_cast<uint32_t>((j - 1) / kLoStages) & 1u,
+                               abort_flag, a.status, a.timeout_cycles);
         if (!ok) break;
         tc_fence_after();
         pv(j - 1);
@@ -425,7 +432,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
     }
     if (ok) {
       ok = mbar_wait_bounded(&sm.p_ready, static_cast<uint32_t>(ntiles - 1) & 1u, abort_flag, a.status,
-                             a.timeout_cycles);
+                             a.timeout_cycles) &&
+           mbar_wait_bounded(&sm.v_ready[(ntiles - 1) % kLoStages], static_cast<uint32_t>((ntiles - 1) / kLoStages) & 1u,
+                             abort_flag, a.status, a.timeout_cycles);
       if (ok) {
         tc_fence_after();
         pv(ntiles - 1);

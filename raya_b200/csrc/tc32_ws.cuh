@@ -1,0 +1,386 @@
+// tc32_ws.cuh — 3xTF32 tensor-core attention with two MMA-issuing warps and
+// the O accumulator in tensor memory (sm_100a).
+//
+// The arithmetic of tc32_pipe_fwd (raw fp32 tiles as the hi operands, lo =
+// x - trunc(x), three tcgen05.mma products per tile), with the two changes
+// that its measurements asked for:
+//
+//   * Two issuing threads.  One thread issuing tcgen05.mma kind::tf32 at
+//     M = 128, N = 64 sustains one instruction per ~47.5 cycles; two threads
+//     in different warps sustain one per ~33.5, the tensor core's own rate
+//     (about 32).  So QK^T and PV are issued by separate warps, each with
+//     its own commit barriers, and the tensor core interleaves the streams.
+//   * O in tensor memory.  PV(j) accumulates straight into an O block of
+//     tensor memory (the first PV of the CTA overwrites it).  The softmax
+//     thread keeps a running log2-domain max m and rescales O (tcgen05.ld,
+//     multiply, tcgen05.st of its own row) only when a tile raises m by more
+//     than 2^8; otherwise it keeps the old m, so weights reach at most 256,
+//     and O and the row sum l stay on the same scale, which the final O / l
+//     removes.  Without o[64] in registers the softmax rows fit the register
+//     budget of a 384-thread block.
+//
+// Roles (384 threads):
+//   warps 0-3   softmax: one query row per thread (TMEM lane = row): q and
+//               its lo part into tensor memory; per key tile: S row -> mask
+//               -> online softmax -> (rare) O rescale -> p and its lo part
+//               into tensor memory; at the end O / l to global memory.
+//   warps 4-9   split: raw K/V tiles by TMA (ring of 4, the hi operands),
+//               their lo parts (ring of 3; K's signalled first), V rows at or
+//               past valid_len zeroed, refills into stages PV(j-3) released.
+//   warp 10     QK issuer: QK(j) into S[j%2] once K's lo part is ready and
+//               S[j%2] has been read.
+//   warp 11     PV issuer: PV(j) into O once P(j) and V's lo part are ready.
+//
+// Tensor memory (512 columns): S0 [0,64), S1 [64,128), Q hi [128,192),
+// Q lo [192,256), P hi [256,320), P lo [320,384), O [384,448).  Every wait
+// is bounded; every group's exit is a collective decision of that group;
+// after a timeout the issuing threads drain their copies and MMAs (bounded)
+// before tensor memory is freed.
+#pragma once
+
+#include "tc32_pipe.cuh"
+
+namespace raya {
+namespace tc32 {
+
+constexpr int kWsThreads = 384;
+constexpr int kWsSplitThreads = 192;  // warps 4-9
+constexpr int kWsQkThread = 320;      // warp 10, lane 0
+constexpr int kWsPvThread = 352;      // warp 11, lane 0
+constexpr float kRescaleLog2 = 8.0f;  // rescale O when the running max grows by more than 2^8
+
+__global__ void __launch_bounds__(kWsThreads, 1)
+    tc32_ws_fwd(const __grid_constant__ AttnArgs a, const __grid_constant__ PipeMaps maps) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw_addr = smem_addr(smem_raw);
+  PipeSmem& sm = *reinterpret_cast<PipeSmem*>(smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr));
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tile = static_cast<int>(blockIdx.x % static_cast<unsigned>(a.row_tiles));
+  const long long bh = blockIdx.x / static_cast<unsigned>(a.row_tiles);
+  const int b = static_cast<int>(bh / a.heads);
+  const int seq = a.seq;
+  int valid = a.valid_len ? a.valid_len[b] : seq;
+  valid = valid < 0 ? 0 : (valid > seq ? seq : valid);
+  const int r0 = tile * kBM;
+  const long long row_base = bh * seq;
+  float* __restrict__ outp = a.out + static_cast<size_t>(row_base) * kD;
+
+  int klo = 0, khi = 0, unused = 0;
+  const int last = min(r0 + kBM, valid) - 1;
+  if (r0 < valid) {
+    key_range(a, r0, valid, klo, unused);
+    key_range(a, last, valid, unused, khi);
+  }
+  const int t_begin = klo / kBN;
+  const int ntiles = khi > klo ? (khi + kBN - 1) / kBN - t_begin : 0;
+
+  if (r0 >= valid || ntiles <= 0) {  // padding only: exact zeros, no loads, no tensor memory
+    const int rows = min(kBM, seq - r0);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int idx = tid; idx < rows * 16; idx += kWsThreads)
+      st_stream(outp + static_cast<size_t>(r0 + (idx >> 4)) * kD + (idx & 15) * 4, zero);
+    return;
+  }
+
+  if (warp == 10) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&sm.tmem_base)),
+                 "r"(kPipeTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    for (int s = 0; s < kRawStages; ++s) mbar_init(&sm.raw_full[s], 1);
+    for (int s = 0; s < kLoStages; ++s) {
+      mbar_init(&sm.k_ready[s], kWsSplitThreads);
+      mbar_init(&sm.v_ready[s], kWsSplitThreads);
+      mbar_init(&sm.kv_free[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.s_full[s], 1);
+      mbar_init(&sm.s_free[s], 128);
+    }
+    mbar_init(&sm.p_ready, 128);
+    mbar_init(&sm.pv_done, 1);
+    mbar_init(&sm.q_ready, 128);
+    sm.abort_flag = 0;
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* abort_flag = &sm.abort_flag;
+
+  // Drain bookkeeping (registers of the issuing threads).
+  int last_tma_tile = -1;
+  uint64_t* last_commit = nullptr;
+  uint32_t last_commit_parity = 0;
+  auto commit = [&](uint64_t* bar, uint32_t parity) {
+    mma_commit(bar);
+    last_commit = bar;
+    last_commit_parity = parity;
+  };
+
+  if (warp < 4) {
+    // ---------------- softmax warpgroup ----------------
+    const int row = r0 + tid;
+    int rlo = 0, rhi = 0;
+    key_range(a, min(row, last), valid, rlo, rhi);
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const float qscale = a.qscale;
+    {  // q row -> tensor memory: q itself (read as its hi part) and q - trunc(q)
+      const float4* src = reinterpret_cast<const float4*>(a.q + static_cast<size_t>(row_base + row) * kD);
+      float h[32], l[32];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 x = row < valid ? __ldg(src + half * 8 + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+          h[4 * c4] = x.x;
+          h[4 * c4 + 1] = x.y;
+          h[4 * c4 + 2] = x.z;
+          h[4 * c4 + 3] = x.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) l[i] = tf32_lo(h[i]);
+        tmem_st32(tmem + lane_off + kColQh + 32 * half, h);
+        tmem_st32(tmem + lane_off + kColQl + 32 * half, l);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&sm.q_ready);
+    }
+
+    float m_used = -INFINITY, lsum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int s = j & 1;
+      const int kt = (t_begin + j) * kBN;
+      bool w = mbar_wait_bounded(&sm.s_full[s], static_cast<uint32_t>(j >> 1) & 1u, abort_flag, a.status,
+                                 a.timeout_cycles);
+      if (__any_sync(0xffffffffu, !w)) { ok = false; break; }
+      tc_fence_after();
+      float sv[64];
+      tmem_ld32(tmem + lane_off + kColS + 64 * s, sv);
+      tmem_ld32(tmem + lane_off + kColS + 64 * s + 32, sv + 32);
+      tc_fence_before();
+      mbar_arrive(&sm.s_free[s]);
+
+      if (!(rlo <= kt && rhi >= kt + kBN)) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (static_cast<unsigned>(kt + c - rlo) >= static_cast<unsigned>(rhi - rlo)) sv[c] = -INFINITY;
+      }
+      float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+      for (int c = 4; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], sv[c]);
+      const float mc = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * qscale;
+      // Move the running max only when it grows by more than 2^8 (or is
+      // first set): O and l are then rescaled by alpha; otherwise weights
+      // stay below 2^8 relative to the kept max.
+      float alpha = 1.f;
+      if (mc > m_used + kRescaleLog2) {
+        alpha = ex2(m_used - mc);  // 0 when m_used was -inf
+        m_used = mc;
+      }
+      const float mbase = m_used == -INFINITY ? 0.f : m_used;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; c += 4) {
+        sv[c] = ex2(fmaf(sv[c], qscale, -mbase));
+        sv[c + 1] = ex2(fmaf(sv[c + 1], qscale, -mbase));
+        sv[c + 2] = ex2(fmaf(sv[c + 2], qscale, -mbase));
+        sv[c + 3] = ex2(fmaf(sv[c + 3], qscale, -mbase));
+        rs += (sv[c] + sv[c + 1]) + (sv[c + 2] + sv[c + 3]);
+      }
+      lsum = fmaf(lsum, alpha, rs);
+
+      if (j > 0) {  // PV(j-1) is complete: P is free and O holds tiles 0..j-1
+        w = mbar_wait_bounded(&sm.pv_done, static_cast<uint32_t>(j - 1) & 1u, abort_flag, a.status,
+                              a.timeout_cycles);
+        if (__any_sync(0xffffffffu, !w)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {  // O row *= alpha (lanes with alpha 1 are unchanged)
+#pragma unroll
+          for (int c = 0; c < 64; c += 32) {
+            float t[32];
+            tmem_ld32(tmem + lane_off + kColPV + c, t);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] *= alpha;
+            tmem_st32(tmem + lane_off + kColPV + c, t);
+          }
+        }
+      }
+      // P -> tensor memory: p itself (read as its hi part), then p - trunc(p) in place.
+      tmem_st32(tmem + lane_off + kColPh, sv);
+      tmem_st32(tmem + lane_off + kColPh + 32, sv + 32);
+#pragma unroll
+      for (int c = 0; c < 64; ++c) sv[c] = tf32_lo(sv[c]);
+      tmem_st32(tmem + lane_off + kColPl, sv);
+      tmem_st32(tmem + lane_off + kColPl + 32, sv + 32);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&sm.p_ready);
+    }
+    float o[64];
+#pragma unroll
+    for (int c = 0; c < 64; ++c) o[c] = 0.f;
+    if (ok) {
+      const bool w = mbar_wait_bounded(&sm.pv_done, static_cast<uint32_t>(ntiles - 1) & 1u, abort_flag, a.status,
+                                       a.timeout_cycles);
+      if (!__any_sync(0xffffffffu, !w)) {
+        tc_fence_after();
+        tmem_ld32(tmem + lane_off + kColPV, o);
+        tmem_ld32(tmem + lane_off + kColPV + 32, o + 32);
+      }
+    }
+    if (row < seq) {  // this row, normalised (+0.0f past valid_len)
+      const float inv = (row < valid && lsum > 0.f) ? 1.0f / lsum : 0.f;
+      float* orow = outp + static_cast<size_t>(row) * kD;
+#pragma unroll
+      for (int c = 0; c < 64; c += 4) {
+        const float4 x = row < valid ? make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        st_stream(orow + c, x);
+      }
+    }
+  } else if (warp < 10) {
+    // ---------------- split warps ----------------
+    const int st = tid - 128;
+    auto issue = [&](int jj) {  // tile jj -> raw stage jj % 4
+      const int s = jj & (kRawStages - 1);
+      uint64_t* bar = &sm.raw_full[s];
+      const int y = static_cast<int>(row_base + (t_begin + jj) * kBN);
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(bar, 2u * kBN * kD * 4u);
+      tiled64::tma_load_2d(&sm.raw[s][0][0][0][0], &maps.k, 0, y, bar);
+      tiled64::tma_load_2d(&sm.raw[s][0][1][0][0], &maps.k, 32, y, bar);
+      tiled64::tma_load_2d(&sm.raw[s][1][0][0][0], &maps.v, 0, y, bar);
+      tiled64::tma_load_2d(&sm.raw[s][1][1][0][0], &maps.v, 32, y, bar);
+      last_tma_tile = jj;
+    };
+    if (st == 0)
+      for (int jj = 0; jj < kRawStages && jj < ntiles; ++jj) issue(jj);
+    for (int j = 0; j < ntiles; ++j) {
+      const int s3 = j % kLoStages, s4 = j & (kRawStages - 1);
+      bool w = true;
+      if (j >= kLoStages) {  // PV(j-3) is done: lo stage s3 and raw stage (j+1)%4 are free
+        w = mbar_wait_bounded(&sm.kv_free[s3], static_cast<uint32_t>(j / kLoStages - 1) & 1u, abort_flag,
+                              a.status, a.timeout_cycles);
+        if (w && st == 0 && j + 1 < ntiles) issue(j + 1);
+      }
+      w = w && mbar_wait_bounded(&sm.raw_full[s4], static_cast<uint32_t>(j >> 2) & 1u, abort_flag, a.status,
+                                 a.timeout_cycles);
+      if (bar_any(kSplitBarrier, kWsSplitThreads, !w)) break;
+      const int nv = min(kBN, valid - (t_begin + j) * kBN);
+      float4* kr = reinterpret_cast<float4*>(&sm.raw[s4][0][0][0][0]);
+      float4* vr = reinterpret_cast<float4*>(&sm.raw[s4][1][0][0][0]);
+      float4* kl = reinterpret_cast<float4*>(&sm.lo[s3][0][0][0][0]);
+      float4* vl = reinterpret_cast<float4*>(&sm.lo[s3][1][0][0][0]);
+#pragma unroll 2
+      for (int f = st; f < kBN * 16; f += kWsSplitThreads) {
+        const float4 x = kr[f];
+        kl[f] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+      }
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+      mbar_arrive(&sm.k_ready[s3]);  // QK(j) may start; V's lo part follows
+      if (nv == kBN) {
+#pragma unroll 2
+        for (int f = st; f < kBN * 16; f += kWsSplitThreads) {
+          const float4 x = vr[f];
+          vl[f] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+        }
+      } else {  // the tail tile: V rows at or past valid_len become exact zeros in both parts
+        for (int f = st; f < kBN * 16; f += kWsSplitThreads) {
+          const int key = (f % (kBN * 8)) >> 3;
+          if (key < nv) {
+            const float4 x = vr[f];
+            vl[f] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+          } else {
+            vr[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+            vl[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&sm.v_ready[s3]);
+      bar_named(kSplitBarrier, kWsSplitThreads);
+    }
+  } else if (tid == kWsQkThread) {
+    // ---------------- QK^T issuer ----------------
+    bool ok = mbar_wait_bounded(&sm.q_ready, 0, abort_flag, a.status, a.timeout_cycles);
+    for (int j = 0; ok && j < ntiles; ++j) {
+      const int s = j & 1, s3 = j % kLoStages;
+      ok = mbar_wait_bounded(&sm.k_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u, abort_flag, a.status,
+                             a.timeout_cycles);
+      if (ok && j >= 2)
+        ok = mbar_wait_bounded(&sm.s_free[s], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag, a.status,
+                               a.timeout_cycles);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t khi = smem_addr(&sm.raw[j & (kRawStages - 1)][0][0][0][0]);
+      const uint32_t klo = smem_addr(&sm.lo[s3][0][0][0][0]);
+      const uint32_t d = tmem + kColS + 64 * s;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kColQh + 8 * k, k_desc(klo, k), kIdescQK, k > 0 ? 1u : 0u);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kColQl + 8 * k, k_desc(khi, k), kIdescQK, 1u);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kColQh + 8 * k, k_desc(khi, k), kIdescQK, 1u);
+      commit(&sm.s_full[s], static_cast<uint32_t>(j >> 1) & 1u);
+    }
+  } else if (tid == kWsPvThread) {
+    // ---------------- PV issuer ----------------
+    bool ok = true;
+    for (int j = 0; ok && j < ntiles; ++j) {
+      const int s3 = j % kLoStages;
+      ok = mbar_wait_bounded(&sm.p_ready, static_cast<uint32_t>(j) & 1u, abort_flag, a.status, a.timeout_cycles) &&
+           mbar_wait_bounded(&sm.v_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u, abort_flag, a.status,
+                             a.timeout_cycles);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t vh = smem_addr(&sm.raw[j & (kRawStages - 1)][1][0][0][0]);
+      const uint32_t vl = smem_addr(&sm.lo[s3][1][0][0][0]);
+      const uint32_t d = tmem + kColPV;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        mma_tf32_ts(d, tmem + kColPh + 8 * k, v_desc(vl, k), kIdescPV, (j > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kColPl + 8 * k, v_desc(vh, k), kIdescPV, 1u);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kColPh + 8 * k, v_desc(vh, k), kIdescPV, 1u);
+      commit(&sm.pv_done, static_cast<uint32_t>(j) & 1u);
+      if (j + kLoStages < ntiles) commit(&sm.kv_free[s3], static_cast<uint32_t>(j / kLoStages) & 1u);
+    }
+  }
+  __syncwarp();
+
+  // Release tensor memory (every path); after a timeout first drain this
+  // CTA's copies and MMAs still in flight (bounded).
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    const long long t0 = clock64();
+    auto drain = [&](uint64_t* bar, uint32_t parity) {
+      while (!mbar_try_wait(bar, parity) && clock64() - t0 < a.timeout_cycles) {
+      }
+    };
+    if (tid == 128) {  // the last tile issued into each raw stage
+#pragma unroll
+      for (int s = 0; s < kRawStages; ++s) {
+        const int t = last_tma_tile - ((last_tma_tile - s) & (kRawStages - 1));
+        if (t >= 0) drain(&sm.raw_full[s], static_cast<uint32_t>(t >> 2) & 1u);
+      }
+    }
+    if ((tid == kWsQkThread || tid == kWsPvThread) && last_commit) drain(last_commit, last_commit_parity);
+  }
+  __syncthreads();
+  if (warp == 10) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPipeTmemCols) : "memory");
+  }
+}
+
+}  // namespace tc32
+}  // namespace raya

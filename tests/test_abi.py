@@ -176,14 +176,14 @@ def test_packed_call_validates_on_the_host():
     (rb.Mask.FULL, 128, True),
 ])
 def test_automatic_kernel_choice(mask, block, expect_tc):
-    """The host-side rule behind RAYA_KERNEL_AUTO: the pipelined tensor-core
-    kernel where enough of a 128-row CTA's key span is allowed, the tuned FFMA
+    """The host-side rule behind RAYA_KERNEL_AUTO: the tensor-core kernel
+    (RAYA_KERNEL_TC32_WS) where enough of a 128-row CTA's key span is allowed, the tuned FFMA
     kernel else, rowwise for head_dim != 64 (no device work involved)."""
     shape = _shape(heads=2, seq=1024, d=64)
     params = rb.AttnParams.new(mask, 1024, 64, block=block)
     kid = rb.kernel_for(shape, params)
     if expect_tc:
-        assert kid == rb._lib.KERNEL_TC32_PIPE
+        assert kid == rb._lib.KERNEL_TC32_WS
     else:
         assert kid in _lib.KERNEL_TILED64_VARIANTS.values()
     assert rb.kernel_for(_shape(heads=2, seq=1024, d=32), rb.AttnParams.new(mask, 1024, 32, block=block)) \

@@ -18,11 +18,12 @@ from _util import (assert_close, cuda_device_run, cuda_host_run, load_golden,
 
 pytestmark = pytest.mark.gpu
 
-KERNELS_D64 = [rb.KERNEL_TILED64, rb.KERNEL_ROWWISE, rb.KERNEL_TC32, rb._lib.KERNEL_TC32_PIPE]
+KERNELS_D64 = [rb.KERNEL_TILED64, rb.KERNEL_ROWWISE, rb.KERNEL_TC32, rb._lib.KERNEL_TC32_PIPE,
+               rb._lib.KERNEL_TC32_WS]
 # every compiled variant of the tiled kernel (warps per CTA x K/V stages)
 TILED_VARIANTS = [rb.KERNEL_TILED64] + sorted(rb._lib.KERNEL_TILED64_VARIANTS.values())
 # every head_dim-64 kernel: the FFMA variants, rowwise, and the 3xTF32 tensor-core kernels
-ALL_D64 = TILED_VARIANTS + [rb.KERNEL_ROWWISE, rb.KERNEL_TC32, rb._lib.KERNEL_TC32_PIPE]
+ALL_D64 = TILED_VARIANTS + [rb.KERNEL_ROWWISE, rb.KERNEL_TC32, rb._lib.KERNEL_TC32_PIPE, rb._lib.KERNEL_TC32_WS]
 B3 = dict(mask=oracle.MASK_BLOCK, block=128, halo=1)
 W64 = dict(mask=oracle.MASK_WINDOW, window=64)
 
@@ -96,7 +97,8 @@ def test_masks_are_exact(cuda_device, mask, d):
     p = oracle.Problem(1, 1, n, d, **mask)
     q, k = oracle.rand_vec(p.numel, 5), oracle.rand_vec(p.numel, 6)
     m = rb.Mask.BLOCK3 if mask is B3 else rb.Mask.WINDOW64
-    kernels = [rb.KERNEL_AUTO] + ([rb.KERNEL_ROWWISE, rb.KERNEL_TC32, rb._lib.KERNEL_TC32_PIPE] if d == 64 else [])
+    kernels = [rb.KERNEL_AUTO] + ([rb.KERNEL_ROWWISE, rb.KERNEL_TC32, rb._lib.KERNEL_TC32_PIPE,
+                                   rb._lib.KERNEL_TC32_WS] if d == 64 else [])
     for kernel in kernels:
         for j in [0, 1, 63, 64, 65, 127, 128, 129, 191, 255, 256, 299]:
             v = np.zeros(p.numel, dtype=np.float32)
