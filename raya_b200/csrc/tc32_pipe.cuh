@@ -65,6 +65,8 @@ struct PipeSmem {
   float raw[kRawStages][2][2][kBN][32];  // [stage][K, V][column half][key][32]: TMA targets = hi operands
   float lo[kLoStages][2][2][kBN][32];    // [stage][K lo, V lo][half][key][32]
   uint64_t raw_full[kRawStages], k_ready[kLoStages], v_ready[kLoStages], kv_free[kLoStages], s_full[2], s_free[2];
+  uint64_t k_free[kLoStages], v_free[kLoStages];  // tc32_ws_fwd: K and V stages released separately
+  uint64_t p_ready2[2], pv_done2[2];              // tc32_ws_fwd: one per P buffer
   uint64_t p_ready, pv_done, q_ready;
   uint32_t tmem_base;
   int abort_flag;

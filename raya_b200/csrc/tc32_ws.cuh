@@ -24,18 +24,29 @@
 //               its lo part into tensor memory; per key tile: S row -> mask
 //               -> online softmax -> (rare) O rescale -> p and its lo part
 //               into tensor memory; at the end O / l to global memory.
-//   warps 4-9   split: raw K/V tiles by TMA (ring of 4, the hi operands),
-//               their lo parts (ring of 3; K's signalled first), V rows at or
-//               past valid_len zeroed, refills into stages PV(j-3) released.
+//   warps 4-9   split: raw K/V tiles by TMA (rings of 4, the hi operands),
+//               their lo parts (ring of 3), V rows at or past valid_len
+//               zeroed.  K and V are released separately: K's lo part of
+//               tile j waits only for QK(j-3) (k_free), V's for PV(j-3)
+//               (v_free), which also frees the raw stage refilled with tile
+//               j+1 (one copy for K and V).  So QK(j) never waits on a PV
+//               product.  (Issuing K's copy ahead of V's, on its own barrier,
+//               measured slower.)
 //   warp 10     QK issuer: QK(j) into S[j%2] once K's lo part is ready and
 //               S[j%2] has been read.
 //   warp 11     PV issuer: PV(j) into O once P(j) and V's lo part are ready.
 //
-// Tensor memory (512 columns): S0 [0,64), S1 [64,128), Q hi [128,192),
-// Q lo [192,256), P hi [256,320), P lo [320,384), O [384,448).  Every wait
-// is bounded; every group's exit is a collective decision of that group;
-// after a timeout the issuing threads drain their copies and MMAs (bounded)
-// before tensor memory is freed.
+// Tensor memory (512 columns): S [0,64), Q hi [64,128), Q lo [128,192),
+// P0 hi/lo [192,320), P1 hi/lo [320,448), O [448,512).  P is double-buffered
+// (the softmax writes P(j) while PV(j-1) still reads P(j-1); only PV(j-2)
+// must be done) and S single-buffered (QK(j+1) starts as soon as the softmax
+// has read S(j), its first step, so it still overlaps the rest of softmax(j)).
+// Writing P over S instead (double-buffering both, QK up to two tiles ahead)
+// measured slower: QK(j+1) then waits for PV(j-1) to complete, later than
+// the softmax's read of S(j).
+// Every wait is bounded; every group's exit is a collective decision of that
+// group; after a timeout the issuing threads drain their copies and MMAs
+// (bounded) before tensor memory is freed.
 #pragma once
 
 #include "tc32_pipe.cuh"
@@ -48,6 +59,9 @@ constexpr int kWsSplitThreads = 192;  // warps 4-9
 constexpr int kWsQkThread = 320;      // warp 10, lane 0
 constexpr int kWsPvThread = 352;      // warp 11, lane 0
 constexpr float kRescaleLog2 = 8.0f;  // rescale O when the running max grows by more than 2^8
+constexpr uint32_t kWsColS = 0, kWsColQh = 64, kWsColQl = 128, kWsColP = 192, kWsColO = 448;
+// P buffer b: hi at kWsColP + 128 b, lo 64 columns further.
+__device__ __forceinline__ uint32_t ws_col_ph(int b) { return kWsColP + 128u * static_cast<uint32_t>(b); }
 
 __global__ void __launch_bounds__(kWsThreads, 1)
     tc32_ws_fwd(const __grid_constant__ AttnArgs a, const __grid_constant__ PipeMaps maps) {
@@ -94,14 +108,15 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     for (int s = 0; s < kLoStages; ++s) {
       mbar_init(&sm.k_ready[s], kWsSplitThreads);
       mbar_init(&sm.v_ready[s], kWsSplitThreads);
-      mbar_init(&sm.kv_free[s], 1);
+      mbar_init(&sm.k_free[s], 1);
+      mbar_init(&sm.v_free[s], 1);
     }
+    mbar_init(&sm.s_full[0], 1);
+    mbar_init(&sm.s_free[0], 128);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.s_free[s], 128);
+      mbar_init(&sm.p_ready2[s], 128);
+      mbar_init(&sm.pv_done2[s], 1);
     }
-    mbar_init(&sm.p_ready, 128);
-    mbar_init(&sm.pv_done, 1);
     mbar_init(&sm.q_ready, 128);
     sm.abort_flag = 0;
     fence_mbar_init();
@@ -113,7 +128,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   volatile int* abort_flag = &sm.abort_flag;
 
   // Drain bookkeeping (registers of the issuing threads).
-  int last_tma_tile = -1;
+  int last_tma_tile = -1;  // split thread 0: last tile copied
   uint64_t* last_commit = nullptr;
   uint32_t last_commit_parity = 0;
   auto commit = [&](uint64_t* bar, uint32_t parity) {
@@ -144,8 +159,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         }
 #pragma unroll
         for (int i = 0; i < 32; ++i) l[i] = tf32_lo(h[i]);
-        tmem_st32(tmem + lane_off + kColQh + 32 * half, h);
-        tmem_st32(tmem + lane_off + kColQl + 32 * half, l);
+        tmem_st32(tmem + lane_off + kWsColQh + 32 * half, h);
+        tmem_st32(tmem + lane_off + kWsColQl + 32 * half, l);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -155,17 +170,17 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     float m_used = -INFINITY, lsum = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      const int s = j & 1;
+      const int pb = j & 1;  // P buffer
       const int kt = (t_begin + j) * kBN;
-      bool w = mbar_wait_bounded(&sm.s_full[s], static_cast<uint32_t>(j >> 1) & 1u, abort_flag, a.status,
+      bool w = mbar_wait_bounded(&sm.s_full[0], static_cast<uint32_t>(j) & 1u, abort_flag, a.status,
                                  a.timeout_cycles);
       if (__any_sync(0xffffffffu, !w)) { ok = false; break; }
       tc_fence_after();
       float sv[64];
-      tmem_ld32(tmem + lane_off + kColS + 64 * s, sv);
-      tmem_ld32(tmem + lane_off + kColS + 64 * s + 32, sv + 32);
+      tmem_ld32(tmem + lane_off + kWsColS, sv);
+      tmem_ld32(tmem + lane_off + kWsColS + 32, sv + 32);
       tc_fence_before();
-      mbar_arrive(&sm.s_free[s]);
+      mbar_arrive(&sm.s_free[0]);  // QK(j+1) may overwrite S
 
       if (!(rlo <= kt && rhi >= kt + kBN)) {
 #pragma unroll
@@ -196,43 +211,50 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
       lsum = fmaf(lsum, alpha, rs);
 
-      if (j > 0) {  // PV(j-1) is complete: P is free and O holds tiles 0..j-1
-        w = mbar_wait_bounded(&sm.pv_done, static_cast<uint32_t>(j - 1) & 1u, abort_flag, a.status,
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // O row *= alpha (lanes with alpha 1 are unchanged), once PV(j-1) is
+        // complete (O then holds tiles 0..j-1).
+        w = mbar_wait_bounded(&sm.pv_done2[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag,
+                              a.status, a.timeout_cycles);
+        if (__any_sync(0xffffffffu, !w)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 64; c += 32) {
+          float t[32];
+          tmem_ld32(tmem + lane_off + kWsColO + c, t);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) t[i] *= alpha;
+          tmem_st32(tmem + lane_off + kWsColO + c, t);
+        }
+      }
+      if (j >= 2) {  // P buffer pb is free once PV(j-2) is complete
+        w = mbar_wait_bounded(&sm.pv_done2[pb], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag, a.status,
                               a.timeout_cycles);
         if (__any_sync(0xffffffffu, !w)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {  // O row *= alpha (lanes with alpha 1 are unchanged)
-#pragma unroll
-          for (int c = 0; c < 64; c += 32) {
-            float t[32];
-            tmem_ld32(tmem + lane_off + kColPV + c, t);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) t[i] *= alpha;
-            tmem_st32(tmem + lane_off + kColPV + c, t);
-          }
-        }
       }
       // P -> tensor memory: p itself (read as its hi part), then p - trunc(p) in place.
-      tmem_st32(tmem + lane_off + kColPh, sv);
-      tmem_st32(tmem + lane_off + kColPh + 32, sv + 32);
+      const uint32_t ph = tmem + lane_off + ws_col_ph(pb);
+      tmem_st32(ph, sv);
+      tmem_st32(ph + 32, sv + 32);
 #pragma unroll
       for (int c = 0; c < 64; ++c) sv[c] = tf32_lo(sv[c]);
-      tmem_st32(tmem + lane_off + kColPl, sv);
-      tmem_st32(tmem + lane_off + kColPl + 32, sv + 32);
+      tmem_st32(ph + 64, sv);
+      tmem_st32(ph + 96, sv + 32);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&sm.p_ready);
+      mbar_arrive(&sm.p_ready2[pb]);
     }
     float o[64];
 #pragma unroll
     for (int c = 0; c < 64; ++c) o[c] = 0.f;
     if (ok) {
-      const bool w = mbar_wait_bounded(&sm.pv_done, static_cast<uint32_t>(ntiles - 1) & 1u, abort_flag, a.status,
-                                       a.timeout_cycles);
+      const bool w = mbar_wait_bounded(&sm.pv_done2[(ntiles - 1) & 1], static_cast<uint32_t>((ntiles - 1) >> 1) & 1u,
+                                       abort_flag, a.status, a.timeout_cycles);
       if (!__any_sync(0xffffffffu, !w)) {
         tc_fence_after();
-        tmem_ld32(tmem + lane_off + kColPV, o);
-        tmem_ld32(tmem + lane_off + kColPV + 32, o + 32);
+        tmem_ld32(tmem + lane_off + kWsColO, o);
+        tmem_ld32(tmem + lane_off + kWsColO + 32, o + 32);
       }
     }
     if (row < seq) {  // this row, normalised (+0.0f past valid_len)
@@ -248,7 +270,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   } else if (warp < 10) {
     // ---------------- split warps ----------------
     const int st = tid - 128;
-    auto issue = [&](int jj) {  // tile jj -> raw stage jj % 4
+    auto issue = [&](int jj) {  // K and V of tile jj -> raw stage jj % 4
       const int s = jj & (kRawStages - 1);
       uint64_t* bar = &sm.raw_full[s];
       const int y = static_cast<int>(row_base + (t_begin + jj) * kBN);
@@ -262,44 +284,54 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     };
     if (st == 0)
       for (int jj = 0; jj < kRawStages && jj < ntiles; ++jj) issue(jj);
+    constexpr int kPer = (kBN * 16 + kWsSplitThreads - 1) / kWsSplitThreads;  // float4s per thread per tile
     for (int j = 0; j < ntiles; ++j) {
       const int s3 = j % kLoStages, s4 = j & (kRawStages - 1);
-      bool w = true;
-      if (j >= kLoStages) {  // PV(j-3) is done: lo stage s3 and raw stage (j+1)%4 are free
-        w = mbar_wait_bounded(&sm.kv_free[s3], static_cast<uint32_t>(j / kLoStages - 1) & 1u, abort_flag,
-                              a.status, a.timeout_cycles);
-        if (w && st == 0 && j + 1 < ntiles) issue(j + 1);
-      }
-      w = w && mbar_wait_bounded(&sm.raw_full[s4], static_cast<uint32_t>(j >> 2) & 1u, abort_flag, a.status,
+      const uint32_t ph = static_cast<uint32_t>(j / kLoStages - 1) & 1u;  // phase of tile j-3's release
+      // K: the raw tile and K's lo stage (QK(j-3) done).
+      bool w = mbar_wait_bounded(&sm.raw_full[s4], static_cast<uint32_t>(j >> 2) & 1u, abort_flag, a.status,
                                  a.timeout_cycles);
+      if (w && j >= kLoStages) w = mbar_wait_bounded(&sm.k_free[s3], ph, abort_flag, a.status, a.timeout_cycles);
       if (bar_any(kSplitBarrier, kWsSplitThreads, !w)) break;
       const int nv = min(kBN, valid - (t_begin + j) * kBN);
       float4* kr = reinterpret_cast<float4*>(&sm.raw[s4][0][0][0][0]);
       float4* vr = reinterpret_cast<float4*>(&sm.raw[s4][1][0][0][0]);
       float4* kl = reinterpret_cast<float4*>(&sm.lo[s3][0][0][0][0]);
       float4* vl = reinterpret_cast<float4*>(&sm.lo[s3][1][0][0][0]);
-#pragma unroll 2
-      for (int f = st; f < kBN * 16; f += kWsSplitThreads) {
-        const float4 x = kr[f];
-        kl[f] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+      {
+        float4 x[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i)
+          if (st + i * kWsSplitThreads < kBN * 16) x[i] = kr[st + i * kWsSplitThreads];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i)
+          if (st + i * kWsSplitThreads < kBN * 16)
+            kl[st + i * kWsSplitThreads] =
+                make_float4(tf32_lo(x[i].x), tf32_lo(x[i].y), tf32_lo(x[i].z), tf32_lo(x[i].w));
       }
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
-      mbar_arrive(&sm.k_ready[s3]);  // QK(j) may start; V's lo part follows
-      if (nv == kBN) {
-#pragma unroll 2
-        for (int f = st; f < kBN * 16; f += kWsSplitThreads) {
-          const float4 x = vr[f];
-          vl[f] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
-        }
-      } else {  // the tail tile: V rows at or past valid_len become exact zeros in both parts
-        for (int f = st; f < kBN * 16; f += kWsSplitThreads) {
-          const int key = (f % (kBN * 8)) >> 3;
-          if (key < nv) {
-            const float4 x = vr[f];
-            vl[f] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
-          } else {
-            vr[f] = make_float4(0.f, 0.f, 0.f, 0.f);
-            vl[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+      mbar_arrive(&sm.k_ready[s3]);  // QK(j) may start
+      // V: V's lo stage and the raw stage of tile j-3 (PV(j-3) done).
+      if (j >= kLoStages) {
+        w = mbar_wait_bounded(&sm.v_free[s3], ph, abort_flag, a.status, a.timeout_cycles);
+        if (w && st == 0 && j + 1 < ntiles) issue(j + 1);  // raw stage (j+1)%4 held tile j-3
+      }
+      if (bar_any(kSplitBarrier, kWsSplitThreads, !w)) break;
+      {
+        float4 x[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i)
+          if (st + i * kWsSplitThreads < kBN * 16) x[i] = vr[st + i * kWsSplitThreads];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int f = st + i * kWsSplitThreads;
+          if (f < kBN * 16) {
+            if (((f % (kBN * 8)) >> 3) < nv) {
+              vl[f] = make_float4(tf32_lo(x[i].x), tf32_lo(x[i].y), tf32_lo(x[i].z), tf32_lo(x[i].w));
+            } else {  // the tail tile: V rows at or past valid_len become exact zeros in both parts
+              vr[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+              vl[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
           }
         }
       }
@@ -311,47 +343,50 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     // ---------------- QK^T issuer ----------------
     bool ok = mbar_wait_bounded(&sm.q_ready, 0, abort_flag, a.status, a.timeout_cycles);
     for (int j = 0; ok && j < ntiles; ++j) {
-      const int s = j & 1, s3 = j % kLoStages;
+      const int s3 = j % kLoStages;
       ok = mbar_wait_bounded(&sm.k_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u, abort_flag, a.status,
                              a.timeout_cycles);
-      if (ok && j >= 2)
-        ok = mbar_wait_bounded(&sm.s_free[s], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag, a.status,
+      if (ok && j >= 1)  // the softmax has read S(j-1)
+        ok = mbar_wait_bounded(&sm.s_free[0], static_cast<uint32_t>(j - 1) & 1u, abort_flag, a.status,
                                a.timeout_cycles);
       if (!ok) break;
       tc_fence_after();
       const uint32_t khi = smem_addr(&sm.raw[j & (kRawStages - 1)][0][0][0][0]);
       const uint32_t klo = smem_addr(&sm.lo[s3][0][0][0][0]);
-      const uint32_t d = tmem + kColS + 64 * s;
+      const uint32_t d = tmem + kWsColS;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kColQh + 8 * k, k_desc(klo, k), kIdescQK, k > 0 ? 1u : 0u);
+      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kWsColQh + 8 * k, k_desc(klo, k), kIdescQK, k > 0 ? 1u : 0u);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kColQl + 8 * k, k_desc(khi, k), kIdescQK, 1u);
+      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kWsColQl + 8 * k, k_desc(khi, k), kIdescQK, 1u);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kColQh + 8 * k, k_desc(khi, k), kIdescQK, 1u);
-      commit(&sm.s_full[s], static_cast<uint32_t>(j >> 1) & 1u);
+      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kWsColQh + 8 * k, k_desc(khi, k), kIdescQK, 1u);
+      commit(&sm.s_full[0], static_cast<uint32_t>(j) & 1u);
+      if (j + kLoStages < ntiles) commit(&sm.k_free[s3], static_cast<uint32_t>(j / kLoStages) & 1u);
     }
   } else if (tid == kWsPvThread) {
     // ---------------- PV issuer ----------------
     bool ok = true;
     for (int j = 0; ok && j < ntiles; ++j) {
       const int s3 = j % kLoStages;
-      ok = mbar_wait_bounded(&sm.p_ready, static_cast<uint32_t>(j) & 1u, abort_flag, a.status, a.timeout_cycles) &&
+      const int pb = j & 1;
+      ok = mbar_wait_bounded(&sm.p_ready2[pb], static_cast<uint32_t>(j >> 1) & 1u, abort_flag, a.status,
+                             a.timeout_cycles) &&
            mbar_wait_bounded(&sm.v_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u, abort_flag, a.status,
                              a.timeout_cycles);
       if (!ok) break;
       tc_fence_after();
       const uint32_t vh = smem_addr(&sm.raw[j & (kRawStages - 1)][1][0][0][0]);
       const uint32_t vl = smem_addr(&sm.lo[s3][1][0][0][0]);
-      const uint32_t d = tmem + kColPV;
+      const uint32_t d = tmem + kWsColO, aph = tmem + ws_col_ph(pb), apl = aph + 64;
 #pragma unroll
       for (int k = 0; k < 8; ++k)
-        mma_tf32_ts(d, tmem + kColPh + 8 * k, v_desc(vl, k), kIdescPV, (j > 0 || k > 0) ? 1u : 0u);
+        mma_tf32_ts(d, aph + 8 * k, v_desc(vl, k), kIdescPV, (j > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kColPl + 8 * k, v_desc(vh, k), kIdescPV, 1u);
+      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, apl + 8 * k, v_desc(vh, k), kIdescPV, 1u);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kColPh + 8 * k, v_desc(vh, k), kIdescPV, 1u);
-      commit(&sm.pv_done, static_cast<uint32_t>(j) & 1u);
-      if (j + kLoStages < ntiles) commit(&sm.kv_free[s3], static_cast<uint32_t>(j / kLoStages) & 1u);
+      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, aph + 8 * k, v_desc(vh, k), kIdescPV, 1u);
+      commit(&sm.pv_done2[pb], static_cast<uint32_t>(j >> 1) & 1u);
+      if (j + kLoStages < ntiles) commit(&sm.v_free[s3], static_cast<uint32_t>(j / kLoStages) & 1u);
     }
   }
   __syncwarp();
