@@ -217,6 +217,22 @@ raya_attn_status encode_rows64(CUtensorMap* map, const float* base, uint64_t row
   return RAYA_ATTN_OK;
 }
 
+// A 3-D tensor map over a [slices][seq][64] fp32 tensor with boxes of
+// [1][64 rows][32 floats], 128-byte swizzle: a store clips rows past seq.
+raya_attn_status encode_slices3d(CUtensorMap* map, float* base, uint64_t slices, uint64_t seq) {
+  raya_attn_status st = load_encoder();
+  if (st != RAYA_ATTN_OK) return st;
+  const cuuint64_t gdim[3] = {64, seq, slices};
+  const cuuint64_t gstride[2] = {64 * sizeof(float), seq * 64 * sizeof(float)};
+  const cuuint32_t box[3] = {32, 64, 1};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, gdim, gstride, box, estride,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(RAYA_ATTN_ERR_CUDA, "cuda: cuTensorMapEncodeTiled (slices) failed (%d)", static_cast<int>(r));
+  return RAYA_ATTN_OK;
+}
+
 // A 4-D tensor map over the packed projection [rows][3][heads][64] fp32
 // (rows = batch*seq) with boxes of [box_rows][1][1][32 floats]: one head of
 // one of q/k/v at box_rows consecutive positions, 128-byte swizzle.
@@ -377,6 +393,8 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     const uint64_t rows = static_cast<uint64_t>(d->batch) * d->heads * d->seq;
     raya_attn_status st = encode_rows64(&maps.k, k, rows, tc32::kBN);
     if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tc32::kBN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    if (st == RAYA_ATTN_OK)
+      st = encode_slices3d(&maps.o, out, static_cast<uint64_t>(d->batch) * d->heads, static_cast<uint64_t>(d->seq));
     if (st != RAYA_ATTN_OK) return st;
     if (kernel_id == RAYA_KERNEL_TC32_WS)
       tc32::tc32_ws_fwd<<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);

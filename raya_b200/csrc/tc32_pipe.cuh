@@ -56,7 +56,20 @@ constexpr uint32_t kColS = 0, kColQh = 128, kColQl = 192, kColPh = 256, kColPl =
 struct PipeMaps {
   CUtensorMap k;  // [rows][64] fp32, boxes [64][32 floats], 128-byte swizzle of 16-byte chunks
   CUtensorMap v;  // the same with the 128-byte swizzle of 32-byte granules
+  CUtensorMap o;  // out as [slices][seq][64], boxes [1][64][32 floats], 128-byte swizzle (tc32_ws_fwd's stores)
 };
+
+// One TMA tile store from shared memory into a 3-D tensor map (rows past the
+// map's bounds are clipped), tracked by the issuing thread's bulk group.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_commit_and_wait() {
+  asm volatile("cp.async.bulk.commit_group;\n\tcp.async.bulk.wait_group 0;" ::: "memory");
+}
 
 constexpr int kRawStages = 4;
 constexpr int kLoStages = 3;

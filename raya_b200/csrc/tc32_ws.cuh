@@ -59,6 +59,7 @@ constexpr int kWsSplitThreads = 192;  // warps 4-9
 constexpr int kWsQkThread = 320;      // warp 10, lane 0
 constexpr int kWsPvThread = 352;      // warp 11, lane 0
 constexpr float kRescaleLog2 = 8.0f;  // rescale O when the running max grows by more than 2^8
+constexpr int kSoftmaxBarrier = 2;    // named barrier of the softmax warps
 constexpr uint32_t kWsColS = 0, kWsColQh = 64, kWsColQl = 128, kWsColP = 192, kWsColO = 448;
 // P buffer b: hi at kWsColP + 128 b, lo 64 columns further.
 __device__ __forceinline__ uint32_t ws_col_ph(int b) { return kWsColP + 128u * static_cast<uint32_t>(b); }
@@ -95,6 +96,22 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     for (int idx = tid; idx < rows * 16; idx += kWsThreads)
       st_stream(outp + static_cast<size_t>(r0 + (idx >> 4)) * kD + (idx & 15) * 4, zero);
     return;
+  }
+
+  // The softmax threads' q rows, loaded before the set-up below (tensor
+  // memory allocation, barriers) so that their memory latency overlaps it.
+  float qf[64];
+  if (warp < 4) {
+    const int row = r0 + tid;
+    const float4* src = reinterpret_cast<const float4*>(a.q + static_cast<size_t>(row_base + row) * kD);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const float4 x = row < valid ? __ldg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      qf[4 * c] = x.x;
+      qf[4 * c + 1] = x.y;
+      qf[4 * c + 2] = x.z;
+      qf[4 * c + 3] = x.w;
+    }
   }
 
   if (warp == 10) {
@@ -144,24 +161,13 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     key_range(a, min(row, last), valid, rlo, rhi);
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     const float qscale = a.qscale;
-    {  // q row -> tensor memory: q itself (read as its hi part) and q - trunc(q)
-      const float4* src = reinterpret_cast<const float4*>(a.q + static_cast<size_t>(row_base + row) * kD);
-      float h[32], l[32];
+    {  // q row -> tensor memory: q itself (read as its hi part), then q - trunc(q)
+      tmem_st32(tmem + lane_off + kWsColQh, qf);
+      tmem_st32(tmem + lane_off + kWsColQh + 32, qf + 32);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-#pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 x = row < valid ? __ldg(src + half * 8 + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
-          h[4 * c4] = x.x;
-          h[4 * c4 + 1] = x.y;
-          h[4 * c4 + 2] = x.z;
-          h[4 * c4 + 3] = x.w;
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) l[i] = tf32_lo(h[i]);
-        tmem_st32(tmem + lane_off + kWsColQh + 32 * half, h);
-        tmem_st32(tmem + lane_off + kWsColQl + 32 * half, l);
-      }
+      for (int i = 0; i < 64; ++i) qf[i] = tf32_lo(qf[i]);
+      tmem_st32(tmem + lane_off + kWsColQl, qf);
+      tmem_st32(tmem + lane_off + kWsColQl + 32, qf + 32);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&sm.q_ready);
@@ -257,14 +263,31 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         tmem_ld32(tmem + lane_off + kWsColO + 32, o + 32);
       }
     }
-    if (row < seq) {  // this row, normalised (+0.0f past valid_len)
+    // This row, normalised (+0.0f past valid_len), staged in shared memory
+    // (raw stage 0 is idle now: every copy has been split and every product
+    // is complete) under the 128-byte swizzle, then stored by TMA: the
+    // [slices][seq][64] map clips rows past the slice's end.
+    {
       const float inv = (row < valid && lsum > 0.f) ? 1.0f / lsum : 0.f;
-      float* orow = outp + static_cast<size_t>(row) * kD;
+      float* stage = &sm.raw[0][0][0][0][0];  // [half][128 rows][32]
 #pragma unroll
-      for (int c = 0; c < 64; c += 4) {
-        const float4 x = row < valid ? make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv)
+      for (int c4 = 0; c4 < 16; ++c4) {
+        const float4 x = row < valid ? make_float4(o[4 * c4] * inv, o[4 * c4 + 1] * inv, o[4 * c4 + 2] * inv,
+                                                   o[4 * c4 + 3] * inv)
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-        st_stream(orow + c, x);
+        sts128(smem_addr(stage) + chunk_offset<kBM>(tid, c4), x);
+      }
+      fence_proxy_async_smem();
+      bar_named(kSoftmaxBarrier, 128);
+      if (tid == 0) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+          for (int rb = 0; rb < 2; ++rb)
+            if (r0 + 64 * rb < seq)  // (a box starting past the slice would be clipped whole; skip it)
+              tma_store_3d(&maps.o, stage + half * kBM * 32 + rb * 64 * 32, 32 * half, r0 + 64 * rb,
+                           static_cast<int>(bh));
+        tma_store_commit_and_wait();
       }
     }
   } else if (warp < 10) {
