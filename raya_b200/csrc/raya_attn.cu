@@ -395,6 +395,7 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tc32::kBN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     if (st == RAYA_ATTN_OK)
       st = encode_slices3d(&maps.o, out, static_cast<uint64_t>(d->batch) * d->heads, static_cast<uint64_t>(d->seq));
+    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.q, q, rows, tc32::kBN);
     if (st != RAYA_ATTN_OK) return st;
     if (kernel_id == RAYA_KERNEL_TC32_WS)
       tc32::tc32_ws_fwd<<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);

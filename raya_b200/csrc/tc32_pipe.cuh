@@ -57,6 +57,7 @@ struct PipeMaps {
   CUtensorMap k;  // [rows][64] fp32, boxes [64][32 floats], 128-byte swizzle of 16-byte chunks
   CUtensorMap v;  // the same with the 128-byte swizzle of 32-byte granules
   CUtensorMap o;  // out as [slices][seq][64], boxes [1][64][32 floats], 128-byte swizzle (tc32_ws_fwd's stores)
+  CUtensorMap q;  // q as [rows][64], boxes [64][32 floats], 128-byte swizzle (tc32_ws_fwd's q tile)
 };
 
 // One TMA tile store from shared memory into a 3-D tensor map (rows past the
@@ -67,8 +68,10 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
                "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
-__device__ __forceinline__ void tma_store_commit_and_wait() {
-  asm volatile("cp.async.bulk.commit_group;\n\tcp.async.bulk.wait_group 0;" ::: "memory");
+// Commits the issuing thread's bulk stores and waits until their shared-memory
+// sources have been read (the global writes complete on their own).
+__device__ __forceinline__ void tma_store_commit_and_wait_read() {
+  asm volatile("cp.async.bulk.commit_group;\n\tcp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 constexpr int kRawStages = 4;
@@ -80,6 +83,7 @@ struct PipeSmem {
   uint64_t raw_full[kRawStages], k_ready[kLoStages], v_ready[kLoStages], kv_free[kLoStages], s_full[2], s_free[2];
   uint64_t k_free[kLoStages], v_free[kLoStages];  // tc32_ws_fwd: K and V stages released separately
   uint64_t p_ready2[2], pv_done2[2];              // tc32_ws_fwd: one per P buffer
+  uint64_t q_full;                                // tc32_ws_fwd: the q tile landed
   uint64_t p_ready, pv_done, q_ready;
   uint32_t tmem_base;
   int abort_flag;

@@ -98,22 +98,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     return;
   }
 
-  // The softmax threads' q rows, loaded before the set-up below (tensor
-  // memory allocation, barriers) so that their memory latency overlaps it.
-  float qf[64];
-  if (warp < 4) {
-    const int row = r0 + tid;
-    const float4* src = reinterpret_cast<const float4*>(a.q + static_cast<size_t>(row_base + row) * kD);
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const float4 x = row < valid ? __ldg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      qf[4 * c] = x.x;
-      qf[4 * c + 1] = x.y;
-      qf[4 * c + 2] = x.z;
-      qf[4 * c + 3] = x.w;
-    }
-  }
-
   if (warp == 10) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&sm.tmem_base)),
                  "r"(kPipeTmemCols)
@@ -135,8 +119,28 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       mbar_init(&sm.pv_done2[s], 1);
     }
     mbar_init(&sm.q_ready, 128);
+    mbar_init(&sm.q_full, 1);
     sm.abort_flag = 0;
     fence_mbar_init();
+    // The first copies leave before the CTA-wide barrier: the q tile (into
+    // lo stage 2, which the split warps first write for key tile 2, after
+    // q_ready) and the K/V tiles of the first four raw stages.
+    float* qs = &sm.lo[2][0][0][0][0];  // [half][128 rows][32]
+    mbar_arrive_expect_tx(&sm.q_full, kBM * kD * 4u);
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+#pragma unroll
+      for (int rb = 0; rb < 2; ++rb)
+        tiled64::tma_load_2d(qs + half * kBM * 32 + rb * 64 * 32, &maps.q, 32 * half,
+                             static_cast<int>(row_base + r0 + 64 * rb), &sm.q_full);
+    for (int jj = 0; jj < kRawStages && jj < ntiles; ++jj) {
+      const int y = static_cast<int>(row_base + (t_begin + jj) * kBN);
+      mbar_arrive_expect_tx(&sm.raw_full[jj], 2u * kBN * kD * 4u);
+      tiled64::tma_load_2d(&sm.raw[jj][0][0][0][0], &maps.k, 0, y, &sm.raw_full[jj]);
+      tiled64::tma_load_2d(&sm.raw[jj][0][1][0][0], &maps.k, 32, y, &sm.raw_full[jj]);
+      tiled64::tma_load_2d(&sm.raw[jj][1][0][0][0], &maps.v, 0, y, &sm.raw_full[jj]);
+      tiled64::tma_load_2d(&sm.raw[jj][1][1][0][0], &maps.v, 32, y, &sm.raw_full[jj]);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -145,7 +149,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   volatile int* abort_flag = &sm.abort_flag;
 
   // Drain bookkeeping (registers of the issuing threads).
-  int last_tma_tile = -1;  // split thread 0: last tile copied
+  int last_tma_tile = min(kRawStages, ntiles) - 1;  // split thread 0: last tile copied (the first four by thread 0)
   uint64_t* last_commit = nullptr;
   uint32_t last_commit_parity = 0;
   auto commit = [&](uint64_t* bar, uint32_t parity) {
@@ -161,7 +165,18 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     key_range(a, min(row, last), valid, rlo, rhi);
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     const float qscale = a.qscale;
-    {  // q row -> tensor memory: q itself (read as its hi part), then q - trunc(q)
+    {  // q row (staged by TMA) -> tensor memory: q itself (read as its hi part), then q - trunc(q)
+      const bool wq = mbar_wait_bounded(&sm.q_full, 0, abort_flag, a.status, a.timeout_cycles);
+      float qf[64];
+      const uint32_t qs = smem_addr(&sm.lo[2][0][0][0][0]);
+#pragma unroll
+      for (int c4 = 0; c4 < 16; ++c4) {
+        const float4 x = (wq && row < valid) ? lds128(qs + chunk_offset<kBM>(tid, c4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        qf[4 * c4] = x.x;
+        qf[4 * c4 + 1] = x.y;
+        qf[4 * c4 + 2] = x.z;
+        qf[4 * c4 + 3] = x.w;
+      }
       tmem_st32(tmem + lane_off + kWsColQh, qf);
       tmem_st32(tmem + lane_off + kWsColQh + 32, qf + 32);
 #pragma unroll
@@ -287,7 +302,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             if (r0 + 64 * rb < seq)  // (a box starting past the slice would be clipped whole; skip it)
               tma_store_3d(&maps.o, stage + half * kBM * 32 + rb * 64 * 32, 32 * half, r0 + 64 * rb,
                            static_cast<int>(bh));
-        tma_store_commit_and_wait();
+        tma_store_commit_and_wait_read();
       }
     }
   } else if (warp < 10) {
@@ -305,8 +320,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       tiled64::tma_load_2d(&sm.raw[s][1][1][0][0], &maps.v, 32, y, bar);
       last_tma_tile = jj;
     };
-    if (st == 0)
-      for (int jj = 0; jj < kRawStages && jj < ntiles; ++jj) issue(jj);
     constexpr int kPer = (kBN * 16 + kWsSplitThreads - 1) / kWsSplitThreads;  // float4s per thread per tile
     for (int j = 0; j < ntiles; ++j) {
       const int s3 = j % kLoStages, s4 = j & (kRawStages - 1);
@@ -315,6 +328,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       bool w = mbar_wait_bounded(&sm.raw_full[s4], static_cast<uint32_t>(j >> 2) & 1u, abort_flag, a.status,
                                  a.timeout_cycles);
       if (w && j >= kLoStages) w = mbar_wait_bounded(&sm.k_free[s3], ph, abort_flag, a.status, a.timeout_cycles);
+      if (w && j == 2) w = mbar_wait_bounded(&sm.q_ready, 0, abort_flag, a.status, a.timeout_cycles);  // q left lo stage 2
       if (bar_any(kSplitBarrier, kWsSplitThreads, !w)) break;
       const int nv = min(kBN, valid - (t_begin + j) * kBN);
       float4* kr = reinterpret_cast<float4*>(&sm.raw[s4][0][0][0][0]);
@@ -424,7 +438,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       while (!mbar_try_wait(bar, parity) && clock64() - t0 < a.timeout_cycles) {
       }
     };
-    if (tid == 128) {  // the last tile issued into each raw stage
+    if (tid == 128) {  // the q copy, and the last tile issued into each raw stage
+      drain(&sm.q_full, 0);
 #pragma unroll
       for (int s = 0; s < kRawStages; ++s) {
         const int t = last_tma_tile - ((last_tma_tile - s) & (kRawStages - 1));
