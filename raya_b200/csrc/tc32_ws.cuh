@@ -60,6 +60,7 @@ constexpr int kWsQkThread = 320;      // warp 10, lane 0
 constexpr int kWsPvThread = 352;      // warp 11, lane 0
 constexpr float kRescaleLog2 = 8.0f;  // rescale O when the running max grows by more than 2^8
 constexpr int kSoftmaxBarrier = 2;    // named barrier of the softmax warps
+static_assert(kLoStages >= 3, "the q tile is staged in lo stage 2 before the split warps first use it");
 constexpr uint32_t kWsColS = 0, kWsColQh = 64, kWsColQl = 128, kWsColP = 192, kWsColO = 448;
 // P buffer b: hi at kWsColP + 128 b, lo 64 columns further.
 __device__ __forceinline__ uint32_t ws_col_ph(int b) { return kWsColP + 128u * static_cast<uint32_t>(b); }

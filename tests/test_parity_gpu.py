@@ -234,3 +234,21 @@ def test_padding_values_never_reach_the_output(cuda_device, mask, kernel):
     assert np.isfinite(got).all()
     assert_close(got, want, "NaN/Inf padding")
     padded_rows_exact_zero(got, p, valid)
+
+
+@pytest.mark.parametrize("mask", [B3, W64, dict(mask=oracle.MASK_FULL)], ids=["block3", "window64", "full"])
+@pytest.mark.parametrize("kernel", [rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_PIPE, rb.KERNEL_AUTO])
+def test_many_units_per_sm(cuda_device, mask, kernel):
+    """More (slice, 128-row) units than SMs, so several CTAs run on each SM
+    in turn, with padding-only units (valid 0 and short sequences) and ragged
+    tails."""
+    rng = np.random.default_rng(123)
+    batch = 48 if mask is not W64 else 40
+    p = oracle.Problem(batch, 4, 700, 64, **mask)
+    q, k, v = oracle.qkv(p.numel, 4242)
+    valid = [int(x) for x in rng.integers(0, 701, size=batch)]
+    valid[:4] = [0, 1, 700, 129]
+    want = oracle.naive(p, q, k, v, valid)
+    got = cuda_device_run(p, q, k, v, valid=valid, kernel=kernel)
+    assert_close(got, want, f"kernel {kernel}")
+    padded_rows_exact_zero(got, p, valid)
