@@ -262,7 +262,7 @@ def run_b200(args) -> None:
     # the kernel that runs: the automatic choice, or the one asked for
     chosen = rb.kernel_for(shape, params, packed=args.packed) if args.kernel == rb.KERNEL_AUTO else args.kernel
     tiled_ids = set(rb._lib.KERNEL_TILED64_VARIANTS.values()) | {rb.KERNEL_TILED64}
-    TENSOR_KERNELS = (rb.KERNEL_TC32, rb._lib.KERNEL_TC32_PIPE, rb._lib.KERNEL_TC32_WS)
+    TENSOR_KERNELS = (rb.KERNEL_TC32, rb._lib.KERNEL_TC32_PIPE, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_STREAM)
     stream = torch.cuda.current_stream(dev)
 
     # Live FFMA peak of this GPU (the roofline denominator: no FP32 figure is
@@ -421,6 +421,8 @@ def run_b200(args) -> None:
                   if chosen == rb._lib.KERNEL_TC32_PIPE else
                   "tc32_ws, two MMA-issuing warps, O in tensor memory, 3xTF32 tcgen05 (raya_b200/csrc/tc32_ws.cuh), "
                   "kernel id 34" if chosen == rb._lib.KERNEL_TC32_WS else
+                  "tc32_stream, one resident CTA per SM streaming its row tiles, 3xTF32 tcgen05 "
+                  "(raya_b200/csrc/tc32_stream.cuh), kernel id 36" if chosen == rb._lib.KERNEL_TC32_STREAM else
                   f"tiled64 (raya_b200/csrc/tiled64.cuh), kernel id {chosen}",
         "kernel_choice": "automatic (raya_attn_kernel_for)" if args.kernel == rb.KERNEL_AUTO else "--kernel",
         "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "stages": stages,

@@ -73,11 +73,12 @@ typedef struct {
 
 /* Kernel selection for raya_attn_forward_ex (tests and benchmarks). */
 typedef enum {
-  RAYA_KERNEL_AUTO = 0,     /* head_dim 64: the tensor-core kernel RAYA_KERNEL_TC32_WS for Full,
-                               windows of half width >= 64, blocks >= 128 and block masks
-                               with a halo whose allowed keys fill >= half of a 128-row
-                               CTA's key span, else the tuned tiled kernel; other
-                               head_dims: rowwise */
+  RAYA_KERNEL_AUTO = 0,     /* head_dim 64: RAYA_KERNEL_TC32_STREAM for block masks with
+                               halo 0 and block 128 or 256; the tensor-core kernel
+                               RAYA_KERNEL_TC32_WS for Full, windows of half width >= 64,
+                               other blocks >= 128 and block masks with a halo whose
+                               allowed keys fill >= half of a 128-row CTA's key span; else
+                               the tuned tiled kernel; other head_dims: rowwise */
   RAYA_KERNEL_TILED64 = 1,  /* the tuned tiled variant for the mask and block (head_dim 64):
                                W4R16_P2 for block <= 64 and windows, W4R32_P2 for
                                block >= 128 and Full */
@@ -100,7 +101,11 @@ typedef enum {
    * sustains only ~2/3 of the tensor core's rate at N = 64) and the O
    * accumulator in tensor memory, rescaled only when a row's max grows by
    * more than 2^8. */
-  RAYA_KERNEL_TC32_WS = 34
+  RAYA_KERNEL_TC32_WS = 34,
+  /* The same pipeline in one resident CTA per SM that walks its 128-row
+   * tiles back to back: each tile's q copy, key-tile splits and first QK^T
+   * overlap the previous tile's last key tiles and output store. */
+  RAYA_KERNEL_TC32_STREAM = 36
 } raya_kernel_id;
 
 /* Argument checks of validate (attention.rs:128-170), extended to the batch

@@ -22,6 +22,7 @@
 #include "tc32.cuh"
 #include "tc32_pipe.cuh"
 #include "tc32_ws.cuh"
+#include "tc32_stream.cuh"
 #include "tiled64.cuh"
 
 namespace raya {
@@ -91,12 +92,16 @@ int tuned_tiled(const raya_attn_desc* d) {
 // for Full, windows of half width >= 64, blocks >= 128, and block masks with
 // a halo whose allowed keys per row, (2*halo + 1) * block, are at least half
 // of that span.  With halo 0 and blocks below 128 the 64-row tiles of the
-// tuned FFMA kernel waste less and win.
+// tuned FFMA kernel waste less and win.  With halo 0 and blocks of 128 or
+// 256 every 128-row CTA has only 2 or 4 key tiles, and the persistent
+// variant, which overlaps one row tile's set-up and output with the previous
+// one's, wins (1.2x and 1.1x; from 512 on, or at halo >= 1, it loses).
 int auto_kernel(const raya_attn_desc* d) {
   if (d->head_dim != 64) return RAYA_KERNEL_ROWWISE;
   if (d->mask == RAYA_MASK_FULL) return RAYA_KERNEL_TC32_WS;
   if (d->mask == RAYA_MASK_WINDOW) return d->window >= 64 ? RAYA_KERNEL_TC32_WS : tuned_tiled(d);
   const long long blk = d->block, halo = d->halo;
+  if (halo == 0 && blk % tc32::kBM == 0 && blk <= 2 * tc32::kBM) return RAYA_KERNEL_TC32_STREAM;
   if (blk >= tc32::kBM) return RAYA_KERNEL_TC32_WS;
   if (halo == 0) return tuned_tiled(d);
   const long long spanned = (tc32::kBM + blk - 1) / blk + (tc32::kBM % blk != 0 ? 1 : 0);
@@ -172,6 +177,9 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
     e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_ws_fwd),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::pipe_smem_bytes()));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_ws smem)");
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_stream_fwd),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::stream_smem_bytes()));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_stream smem)");
     for (const PackedVariant& pv : kPacked) {
       for (auto fn : {pv.plain, pv.rope}) {
         e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
@@ -381,7 +389,9 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tc32::kBN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     if (st != RAYA_ATTN_OK) return st;
     tc32::tc32_fwd<<<static_cast<unsigned>(grid), tc32::kThreads, tc32::smem_bytes(), stream>>>(a, maps);
-  } else if ((kernel_id == RAYA_KERNEL_TC32_PIPE || kernel_id == RAYA_KERNEL_TC32_WS) && !stage_cycles) {
+  } else if ((kernel_id == RAYA_KERNEL_TC32_PIPE || kernel_id == RAYA_KERNEL_TC32_WS ||
+              kernel_id == RAYA_KERNEL_TC32_STREAM) &&
+             !stage_cycles) {
     if (d->head_dim != 64)
       return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tensor-core kernel needs head_dim 64, got %lld",
                   static_cast<long long>(d->head_dim));
@@ -397,7 +407,14 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
       st = encode_slices3d(&maps.o, out, static_cast<uint64_t>(d->batch) * d->heads, static_cast<uint64_t>(d->seq));
     if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.q, q, rows, tc32::kBN);
     if (st != RAYA_ATTN_OK) return st;
-    if (kernel_id == RAYA_KERNEL_TC32_WS)
+    if (rows > 0x7fffffffull)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %llu rows exceed the tensor-map row limit",
+                  static_cast<unsigned long long>(rows));
+    if (kernel_id == RAYA_KERNEL_TC32_STREAM) {
+      const long long resident = std::min<long long>(grid, ctx->sms);  // one CTA per SM walks the row tiles
+      tc32::tc32_stream_fwd<<<static_cast<unsigned>(resident), tc32::kWsThreads, tc32::stream_smem_bytes(),
+                              stream>>>(a, maps);
+    } else if (kernel_id == RAYA_KERNEL_TC32_WS)
       tc32::tc32_ws_fwd<<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
     else
       tc32::tc32_pipe_fwd<<<static_cast<unsigned>(grid), tc32::kPipeThreads, tc32::pipe_smem_bytes(), stream>>>(

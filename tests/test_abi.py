@@ -164,7 +164,10 @@ def test_packed_call_validates_on_the_host():
 
 @pytest.mark.parametrize("mask,block,expect_tc", [
     (rb.Mask.block(1), 128, True),    # Block3: every allowed key of a 128-row span
-    (rb.Mask.block(0), 256, True),
+    (rb.Mask.block(0), 256, "stream"),  # halo 0, 2-4 key tiles per 128-row tile: the persistent kernel
+    (rb.Mask.block(0), 128, "stream"),
+    (rb.Mask.block(0), 512, True),
+    (rb.Mask.block(0), 192, True),
     (rb.Mask.block(2), 64, True),     # 320 of 384 span keys allowed per row
     (rb.Mask.block(1), 64, True),     # 192 of 256
     (rb.Mask.block(1), 32, True),     # 96 of 192
@@ -177,12 +180,15 @@ def test_packed_call_validates_on_the_host():
 ])
 def test_automatic_kernel_choice(mask, block, expect_tc):
     """The host-side rule behind RAYA_KERNEL_AUTO: the tensor-core kernel
-    (RAYA_KERNEL_TC32_WS) where enough of a 128-row CTA's key span is allowed, the tuned FFMA
+    (RAYA_KERNEL_TC32_WS) where enough of a 128-row CTA's key span is allowed, its persistent
+    variant (RAYA_KERNEL_TC32_STREAM) for halo 0 with blocks of 128 or 256, the tuned FFMA
     kernel else, rowwise for head_dim != 64 (no device work involved)."""
     shape = _shape(heads=2, seq=1024, d=64)
     params = rb.AttnParams.new(mask, 1024, 64, block=block)
     kid = rb.kernel_for(shape, params)
-    if expect_tc:
+    if expect_tc == "stream":
+        assert kid == rb._lib.KERNEL_TC32_STREAM
+    elif expect_tc:
         assert kid == rb._lib.KERNEL_TC32_WS
     else:
         assert kid in _lib.KERNEL_TILED64_VARIANTS.values()
