@@ -335,7 +335,8 @@ def run_b200(args) -> None:
     achieved_tf = flops_launch / (launch_ms * 1e-3) / 1e12
     peaks, peak_kind = load_peaks()
     hbm = peaks.get("hbm_gbs")
-    tkey = f"{w.name}-halo{w.halo}" + (f"-k{chosen}" if chosen in TENSOR_KERNELS else "")
+    tkey = (f"{w.name}-halo{w.halo}" + (f"-k{chosen}" if chosen in TENSOR_KERNELS else "")
+            + ("-packed" if args.packed else ""))
     hbm_obj = {"achieved": round(bytes_launch / (launch_ms * 1e-3) / 1e9, 1), "peak": hbm,
                "unit": "GB/s", "frac": round(bytes_launch / (launch_ms * 1e-3) / 1e9 / hbm, 4) if hbm else None,
                "peak_source": f"MEASURED_PEAKS.json hbm_gbs (of {peak_kind})" if peak_kind == "measured"

@@ -158,7 +158,10 @@ raya_attn_status raya_attn_forward_ex(const raya_attn_desc* desc, const float* q
  * as the reference computes them); 0 skips the rotation.  With rope_theta > 0
  * the call needs a DEVICE workspace of raya_attn_packed_workspace bytes (the
  * cos/sin table, written by the call); it may be NULL otherwise.  head_dim
- * must be 64.  Asynchronous on `stream`; allocates nothing. */
+ * must be 64.  Asynchronous on `stream`; allocates nothing.  Kernel: the
+ * two-issuer tensor-core kernel (RAYA_KERNEL_TC32_WS) with this layout
+ * wherever RAYA_KERNEL_AUTO picks a tensor-core kernel, else the tuned tiled
+ * kernel (raya_attn_kernel_for with packed != 0 names it). */
 raya_attn_status raya_attn_forward_packed(const raya_attn_desc* desc, const float* qkv, float* ctx,
                                           const int32_t* valid_len, float rope_theta, void* workspace,
                                           size_t workspace_bytes, void* stream);

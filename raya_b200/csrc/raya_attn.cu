@@ -110,6 +110,14 @@ int auto_kernel(const raya_attn_desc* d) {
   return 2 * allowed >= span ? RAYA_KERNEL_TC32_WS : tuned_tiled(d);
 }
 
+// The packed entry points' kernel: the two-issuer tensor-core kernel with the
+// packed layout where the automatic choice is a tensor-core kernel (the
+// persistent variant has no packed form), else the tuned tiled kernel.
+int packed_kernel(const raya_attn_desc* d) {
+  const int id = auto_kernel(d);
+  return id == RAYA_KERNEL_TC32_WS || id == RAYA_KERNEL_TC32_STREAM ? RAYA_KERNEL_TC32_WS : tuned_tiled(d);
+}
+
 // Device status word: bit 0 = a bounded wait gave up.  One per device that
 // loads the library; its device address is looked up once per device.
 __device__ int g_status;
@@ -174,9 +182,12 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
     e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_pipe_fwd),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::pipe_smem_bytes()));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_pipe smem)");
-    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_ws_fwd),
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::pipe_smem_bytes()));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_ws smem)");
+    for (auto fn : {tc32::tc32_ws_fwd<tiled64::kHeadMajor, false>, tc32::tc32_ws_fwd<tiled64::kPacked, false>,
+                    tc32::tc32_ws_fwd<tiled64::kPacked, true>}) {
+      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(tc32::pipe_smem_bytes()));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_ws smem)");
+    }
     e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_stream_fwd),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::stream_smem_bytes()));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_stream smem)");
@@ -245,7 +256,7 @@ raya_attn_status encode_slices3d(CUtensorMap* map, float* base, uint64_t slices,
 // (rows = batch*seq) with boxes of [box_rows][1][1][32 floats]: one head of
 // one of q/k/v at box_rows consecutive positions, 128-byte swizzle.
 raya_attn_status encode_packed(CUtensorMap* map, const float* base, uint64_t rows, uint64_t heads,
-                               uint32_t box_rows) {
+                               uint32_t box_rows, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   raya_attn_status st = load_encoder();
   if (st != RAYA_ATTN_OK) return st;
   const cuuint64_t gdim[4] = {64, heads, 3, rows};
@@ -253,9 +264,26 @@ raya_attn_status encode_packed(CUtensorMap* map, const float* base, uint64_t row
   const cuuint32_t box[4] = {32, 1, 1, box_rows};
   const cuuint32_t estride[4] = {1, 1, 1, 1};
   const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), gdim, gstride,
-                              box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(RAYA_ATTN_ERR_CUDA, "cuda: cuTensorMapEncodeTiled (packed) failed (%d)", static_cast<int>(r));
+  return RAYA_ATTN_OK;
+}
+
+// A 4-D tensor map over the context tensor [batch][seq][heads][64] with boxes
+// of [1][64 rows][1][32 floats], 128-byte swizzle: a store clips rows past seq.
+raya_attn_status encode_context(CUtensorMap* map, float* base, uint64_t batch, uint64_t seq, uint64_t heads) {
+  raya_attn_status st = load_encoder();
+  if (st != RAYA_ATTN_OK) return st;
+  const cuuint64_t gdim[4] = {64, heads, seq, batch};
+  const cuuint64_t gstride[3] = {64 * sizeof(float), heads * 64 * sizeof(float), seq * heads * 64 * sizeof(float)};
+  const cuuint32_t box[4] = {32, 1, 64, 1};
+  const cuuint32_t estride[4] = {1, 1, 1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, gdim, gstride, box, estride,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(RAYA_ATTN_ERR_CUDA, "cuda: cuTensorMapEncodeTiled (context) failed (%d)", static_cast<int>(r));
   return RAYA_ATTN_OK;
 }
 
@@ -415,7 +443,8 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
       tc32::tc32_stream_fwd<<<static_cast<unsigned>(resident), tc32::kWsThreads, tc32::stream_smem_bytes(),
                               stream>>>(a, maps);
     } else if (kernel_id == RAYA_KERNEL_TC32_WS)
-      tc32::tc32_ws_fwd<<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
+      tc32::tc32_ws_fwd<tiled64::kHeadMajor, false>
+          <<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
     else
       tc32::tc32_pipe_fwd<<<static_cast<unsigned>(grid), tc32::kPipeThreads, tc32::pipe_smem_bytes(), stream>>>(
           a, maps);
@@ -613,6 +642,56 @@ raya_attn_status raya_attn_forward_timed(const raya_attn_desc* desc, const float
                 reinterpret_cast<unsigned long long*>(stage_cycles));
 }
 
+// The packed layout's attention launch (rope_cs: the (cos, sin) table, or
+// NULL for no rotation), shared by both packed entry points.
+raya_attn_status launch_packed(DeviceCtx* ctx_dev, const raya_attn_desc* desc, const float* qkv, float* ctx,
+                               const int32_t* valid_len, const float* rope_cs, cudaStream_t s) {
+  const bool rope = rope_cs != nullptr;
+  AttnArgs a = make_args(desc, qkv, qkv, qkv, ctx, valid_len, ctx_dev->status);
+  a.rope_cs = rope_cs;
+  const uint64_t rows = static_cast<uint64_t>(desc->batch) * desc->seq;
+  raya_attn_status st;
+  if (packed_kernel(desc) == RAYA_KERNEL_TC32_WS) {
+    a.row_tiles = static_cast<int>((desc->seq + tc32::kBM - 1) / tc32::kBM);
+    const long long grid = static_cast<long long>(desc->batch) * desc->heads * a.row_tiles;
+    if (grid > 0x7fffffffll)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
+    if (rows > 0x7fffffffull)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %llu rows exceed the tensor-map row limit",
+                  static_cast<unsigned long long>(rows));
+    tc32::PipeMaps maps;
+    st = encode_packed(&maps.q, qkv, rows, desc->heads, tc32::kBN);
+    if (st == RAYA_ATTN_OK)
+      st = encode_packed(&maps.v, qkv, rows, desc->heads, tc32::kBN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    if (st == RAYA_ATTN_OK)
+      st = encode_context(&maps.o, ctx, static_cast<uint64_t>(desc->batch), static_cast<uint64_t>(desc->seq),
+                          static_cast<uint64_t>(desc->heads));
+    if (st != RAYA_ATTN_OK) return st;
+    maps.k = maps.q;  // the same [64 rows][32] boxes of the packed tensor
+    (rope ? tc32::tc32_ws_fwd<tiled64::kPacked, true> : tc32::tc32_ws_fwd<tiled64::kPacked, false>)
+        <<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), s>>>(a, maps);
+  } else {
+    const int id = tuned_tiled(desc);
+    const PackedVariant* pv = nullptr;
+    for (const PackedVariant& v : kPacked)
+      if (v.id == id) pv = &v;
+    const int bm = pv->warps * pv->rows_per_warp;
+    a.row_tiles = static_cast<int>((desc->seq + bm - 1) / bm);
+    const long long grid = static_cast<long long>(desc->batch) * desc->heads * a.row_tiles;
+    if (grid > 0x7fffffffll)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
+    tiled64::TmaMaps maps;
+    st = encode_packed(&maps.q, qkv, rows, desc->heads, static_cast<uint32_t>(bm));
+    if (st == RAYA_ATTN_OK) st = encode_packed(&maps.k, qkv, rows, desc->heads, tiled64::kBN);
+    if (st != RAYA_ATTN_OK) return st;
+    maps.v = maps.k;
+    (rope ? pv->rope : pv->plain)<<<static_cast<unsigned>(grid), pv->warps * 32, pv->smem, s>>>(a, maps);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "packed kernel launch");
+  return RAYA_ATTN_OK;
+}
+
 raya_attn_status raya_attn_packed_workspace(const raya_attn_desc* desc, float rope_theta, size_t* bytes) {
   raya_attn_status st = check_shape(desc);
   if (st != RAYA_ATTN_OK) return st;
@@ -656,27 +735,7 @@ raya_attn_status raya_attn_forward_packed(const raya_attn_desc* desc, const floa
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "rope table launch");
   }
-  const int id = tuned_tiled(desc);
-  const PackedVariant* pv = nullptr;
-  for (const PackedVariant& v : kPacked)
-    if (v.id == id) pv = &v;
-  const int bm = pv->warps * pv->rows_per_warp;
-  AttnArgs a = make_args(desc, qkv, qkv, qkv, ctx, valid_len, ctx_dev->status);
-  a.rope_cs = rope ? static_cast<const float*>(workspace) : nullptr;
-  a.row_tiles = static_cast<int>((desc->seq + bm - 1) / bm);
-  const long long grid = static_cast<long long>(desc->batch) * desc->heads * a.row_tiles;
-  if (grid > 0x7fffffffll)
-    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
-  tiled64::TmaMaps maps;
-  const uint64_t rows = static_cast<uint64_t>(desc->batch) * desc->seq;
-  st = encode_packed(&maps.q, qkv, rows, desc->heads, static_cast<uint32_t>(bm));
-  if (st == RAYA_ATTN_OK) st = encode_packed(&maps.k, qkv, rows, desc->heads, tiled64::kBN);
-  if (st != RAYA_ATTN_OK) return st;
-  maps.v = maps.k;
-  (rope ? pv->rope : pv->plain)<<<static_cast<unsigned>(grid), pv->warps * 32, pv->smem, s>>>(a, maps);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "packed kernel launch");
-  return RAYA_ATTN_OK;
+  return launch_packed(ctx_dev, desc, qkv, ctx, valid_len, rope ? static_cast<const float*>(workspace) : nullptr, s);
 }
 
 raya_attn_status raya_attn_forward_packed_noalloc(const raya_attn_desc* desc, const float* qkv, float* ctx,
@@ -722,27 +781,7 @@ raya_attn_status raya_attn_forward_packed_noalloc(const raya_attn_desc* desc, co
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "rope table launch");
   }
-  const int id = tuned_tiled(desc);
-  const PackedVariant* pv = nullptr;
-  for (const PackedVariant& v : kPacked)
-    if (v.id == id) pv = &v;
-  const int bm = pv->warps * pv->rows_per_warp;
-  AttnArgs a = make_args(desc, qkv, qkv, qkv, ctx, valid_len, ctx_dev->status);
-  a.rope_cs = rope ? reinterpret_cast<const float*>(table) : nullptr;
-  a.row_tiles = static_cast<int>((desc->seq + bm - 1) / bm);
-  const long long grid = static_cast<long long>(desc->batch) * desc->heads * a.row_tiles;
-  if (grid > 0x7fffffffll)
-    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
-  tiled64::TmaMaps maps;
-  const uint64_t rows = static_cast<uint64_t>(desc->batch) * desc->seq;
-  st = encode_packed(&maps.q, qkv, rows, desc->heads, static_cast<uint32_t>(bm));
-  if (st == RAYA_ATTN_OK) st = encode_packed(&maps.k, qkv, rows, desc->heads, tiled64::kBN);
-  if (st != RAYA_ATTN_OK) return st;
-  maps.v = maps.k;
-  (rope ? pv->rope : pv->plain)<<<static_cast<unsigned>(grid), pv->warps * 32, pv->smem, s>>>(a, maps);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "packed kernel launch");
-  return RAYA_ATTN_OK;
+  return launch_packed(ctx_dev, desc, qkv, ctx, valid_len, rope ? reinterpret_cast<const float*>(table) : nullptr, s);
 }
 
 raya_attn_status raya_attn_probe_timeout(int64_t timeout_cycles, void* stream) {
@@ -883,8 +922,7 @@ raya_attn_status raya_attn_kernel_for(const raya_attn_desc* desc, int packed, in
   raya_attn_status st = check_shape(desc);
   if (st != RAYA_ATTN_OK) return st;
   if (!kernel) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null kernel pointer");
-  const int id = packed ? RAYA_KERNEL_TILED64 : auto_kernel(desc);
-  *kernel = id == RAYA_KERNEL_TILED64 ? tuned_tiled(desc) : id;
+  *kernel = packed ? packed_kernel(desc) : auto_kernel(desc);
   return RAYA_ATTN_OK;
 }
 

@@ -68,6 +68,13 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
                "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
+// The same into a 4-D tensor map (the packed layout's context tensor).
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
 // Commits the issuing thread's bulk stores and waits until their shared-memory
 // sources have been read (the global writes complete on their own).
 __device__ __forceinline__ void tma_store_commit_and_wait_read() {

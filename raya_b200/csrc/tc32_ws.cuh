@@ -65,8 +65,38 @@ constexpr uint32_t kWsColS = 0, kWsColQh = 64, kWsColQl = 128, kWsColP = 192, kW
 // P buffer b: hi at kWsColP + 128 b, lo 64 columns further.
 __device__ __forceinline__ uint32_t ws_col_ph(int b) { return kWsColP + 128u * static_cast<uint32_t>(b); }
 
+// The copies of a [64 rows][32] column-half box of q (which 0), K (1) or V
+// (2): head-major 2-D maps (column, slice*seq + pos) or the packed 4-D maps
+// (column, head, which, b*seq + pos).
+template <int LAYOUT>
+__device__ __forceinline__ void ws_load(void* dst, const CUtensorMap* map, int x, int head, int which, int y,
+                                        uint64_t* bar) {
+  if constexpr (LAYOUT == tiled64::kHeadMajor)
+    tiled64::tma_load_2d(dst, map, x, y, bar);
+  else
+    tiled64::tma_load_4d(dst, map, x, head, which, y, bar);
+}
+
+// raya's rotary embedding (ops.rs:110-141, rotate-half form) of one element
+// pair: (x, y) -> (x*cos - y*sin, y*cos + x*sin), unfused f32 as the
+// reference computes it (the FFMA kernels' rope_rows does the same).
+__device__ __forceinline__ void ws_rot(float& x, float& y, float c, float sn) {
+  const float nx = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
+  const float ny = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+  x = nx;
+  y = ny;
+}
+
+// LAYOUT: tiled64::kHeadMajor (q, k, v, out as [batch*heads*seq][64]) or
+// tiled64::kPacked (q, k, v read in place from the packed projection
+// [batch*seq][3][heads][64], the output written as the context
+// [batch*seq][heads][64]: encoder.rs:34-92).  ROPE: q and k rotated first
+// (packed layout only), q rows by the softmax warps before they enter tensor
+// memory, K tiles by the split warps before their lo parts are taken.
+template <int LAYOUT, bool ROPE>
 __global__ void __launch_bounds__(kWsThreads, 1)
     tc32_ws_fwd(const __grid_constant__ AttnArgs a, const __grid_constant__ PipeMaps maps) {
+  static_assert(!ROPE || LAYOUT == tiled64::kPacked, "the rotation is fused into the packed layout only");
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
   PipeSmem& sm = *reinterpret_cast<PipeSmem*>(smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr));
@@ -79,8 +109,15 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   int valid = a.valid_len ? a.valid_len[b] : seq;
   valid = valid < 0 ? 0 : (valid > seq ? seq : valid);
   const int r0 = tile * kBM;
-  const long long row_base = bh * seq;
-  float* __restrict__ outp = a.out + static_cast<size_t>(row_base) * kD;
+  const int head = static_cast<int>(bh % a.heads);
+  // First row of this slice in the loads' row coordinate, and the output
+  // rows (head-major: the slice's rows; packed: this head's 64 columns of
+  // each context row).
+  const long long row_base = LAYOUT == tiled64::kHeadMajor ? bh * seq : static_cast<long long>(b) * seq;
+  const size_t out_stride = LAYOUT == tiled64::kHeadMajor ? kD : static_cast<size_t>(a.heads) * kD;
+  float* __restrict__ outp =
+      a.out + (LAYOUT == tiled64::kHeadMajor ? static_cast<size_t>(row_base) * kD
+                                             : (static_cast<size_t>(row_base) * a.heads + head) * kD);
 
   int klo = 0, khi = 0, unused = 0;
   const int last = min(r0 + kBM, valid) - 1;
@@ -95,7 +132,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     const int rows = min(kBM, seq - r0);
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int idx = tid; idx < rows * 16; idx += kWsThreads)
-      st_stream(outp + static_cast<size_t>(r0 + (idx >> 4)) * kD + (idx & 15) * 4, zero);
+      st_stream(outp + static_cast<size_t>(r0 + (idx >> 4)) * out_stride + (idx & 15) * 4, zero);
     return;
   }
 
@@ -132,15 +169,15 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     for (int half = 0; half < 2; ++half)
 #pragma unroll
       for (int rb = 0; rb < 2; ++rb)
-        tiled64::tma_load_2d(qs + half * kBM * 32 + rb * 64 * 32, &maps.q, 32 * half,
-                             static_cast<int>(row_base + r0 + 64 * rb), &sm.q_full);
+        ws_load<LAYOUT>(qs + half * kBM * 32 + rb * 64 * 32, &maps.q, 32 * half, head, 0,
+                        static_cast<int>(row_base + r0 + 64 * rb), &sm.q_full);
     for (int jj = 0; jj < kRawStages && jj < ntiles; ++jj) {
       const int y = static_cast<int>(row_base + (t_begin + jj) * kBN);
       mbar_arrive_expect_tx(&sm.raw_full[jj], 2u * kBN * kD * 4u);
-      tiled64::tma_load_2d(&sm.raw[jj][0][0][0][0], &maps.k, 0, y, &sm.raw_full[jj]);
-      tiled64::tma_load_2d(&sm.raw[jj][0][1][0][0], &maps.k, 32, y, &sm.raw_full[jj]);
-      tiled64::tma_load_2d(&sm.raw[jj][1][0][0][0], &maps.v, 0, y, &sm.raw_full[jj]);
-      tiled64::tma_load_2d(&sm.raw[jj][1][1][0][0], &maps.v, 32, y, &sm.raw_full[jj]);
+      ws_load<LAYOUT>(&sm.raw[jj][0][0][0][0], &maps.k, 0, head, 1, y, &sm.raw_full[jj]);
+      ws_load<LAYOUT>(&sm.raw[jj][0][1][0][0], &maps.k, 32, head, 1, y, &sm.raw_full[jj]);
+      ws_load<LAYOUT>(&sm.raw[jj][1][0][0][0], &maps.v, 0, head, 2, y, &sm.raw_full[jj]);
+      ws_load<LAYOUT>(&sm.raw[jj][1][1][0][0], &maps.v, 32, head, 2, y, &sm.raw_full[jj]);
     }
   }
   tc_fence_before();
@@ -167,6 +204,12 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     const float qscale = a.qscale;
     {  // q row (staged by TMA) -> tensor memory: q itself (read as its hi part), then q - trunc(q)
+      float4 qcs[ROPE ? 16 : 1];  // this row's (cos, sin) pairs, loaded while the q tile is in flight
+      if constexpr (ROPE) {
+        const float4* t = reinterpret_cast<const float4*>(a.rope_cs + static_cast<size_t>(min(row, seq - 1)) * 64);
+#pragma unroll
+        for (int i4 = 0; i4 < 16; ++i4) qcs[i4] = __ldg(t + i4);
+      }
       const bool wq = mbar_wait_bounded(&sm.q_full, 0, abort_flag, a.status, a.timeout_cycles);
       float qf[64];
       const uint32_t qs = smem_addr(&sm.lo[2][0][0][0][0]);
@@ -177,6 +220,15 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         qf[4 * c4 + 1] = x.y;
         qf[4 * c4 + 2] = x.z;
         qf[4 * c4 + 3] = x.w;
+      }
+      if constexpr (ROPE) {
+        if (wq && row < valid) {  // element i with i + 32, (cos, sin) of this position from the table
+#pragma unroll
+          for (int i4 = 0; i4 < 16; ++i4) {  // pairs i = 2*i4, 2*i4 + 1
+            ws_rot(qf[2 * i4], qf[2 * i4 + 32], qcs[i4].x, qcs[i4].y);
+            ws_rot(qf[2 * i4 + 1], qf[2 * i4 + 33], qcs[i4].z, qcs[i4].w);
+          }
+        }
       }
       tmem_st32(tmem + lane_off + kWsColQh, qf);
       tmem_st32(tmem + lane_off + kWsColQh + 32, qf + 32);
@@ -300,9 +352,13 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         for (int half = 0; half < 2; ++half)
 #pragma unroll
           for (int rb = 0; rb < 2; ++rb)
-            if (r0 + 64 * rb < seq)  // (a box starting past the slice would be clipped whole; skip it)
-              tma_store_3d(&maps.o, stage + half * kBM * 32 + rb * 64 * 32, 32 * half, r0 + 64 * rb,
-                           static_cast<int>(bh));
+            if (r0 + 64 * rb < seq) {  // (a box starting past the slice would be clipped whole; skip it)
+              if constexpr (LAYOUT == tiled64::kHeadMajor)
+                tma_store_3d(&maps.o, stage + half * kBM * 32 + rb * 64 * 32, 32 * half, r0 + 64 * rb,
+                             static_cast<int>(bh));
+              else  // [batch][seq][heads][64]: (column, head, pos, b)
+                tma_store_4d(&maps.o, stage + half * kBM * 32 + rb * 64 * 32, 32 * half, head, r0 + 64 * rb, b);
+            }
         tma_store_commit_and_wait_read();
       }
     }
@@ -315,13 +371,35 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int y = static_cast<int>(row_base + (t_begin + jj) * kBN);
       fence_proxy_async_smem();
       mbar_arrive_expect_tx(bar, 2u * kBN * kD * 4u);
-      tiled64::tma_load_2d(&sm.raw[s][0][0][0][0], &maps.k, 0, y, bar);
-      tiled64::tma_load_2d(&sm.raw[s][0][1][0][0], &maps.k, 32, y, bar);
-      tiled64::tma_load_2d(&sm.raw[s][1][0][0][0], &maps.v, 0, y, bar);
-      tiled64::tma_load_2d(&sm.raw[s][1][1][0][0], &maps.v, 32, y, bar);
+      ws_load<LAYOUT>(&sm.raw[s][0][0][0][0], &maps.k, 0, head, 1, y, bar);
+      ws_load<LAYOUT>(&sm.raw[s][0][1][0][0], &maps.k, 32, head, 1, y, bar);
+      ws_load<LAYOUT>(&sm.raw[s][1][0][0][0], &maps.v, 0, head, 2, y, bar);
+      ws_load<LAYOUT>(&sm.raw[s][1][1][0][0], &maps.v, 32, head, 2, y, bar);
       last_tma_tile = jj;
     };
     constexpr int kPer = (kBN * 16 + kWsSplitThreads - 1) / kWsSplitThreads;  // float4s per thread per tile
+    // With the rotation: (cos, sin) of this thread's element pairs of the next
+    // K tile, loaded one tile ahead (float4 f of a column half, f < kBN*8:
+    // row f / 8, logical chunk (f % 8) ^ (row % 8)).
+    constexpr int kPairs = kBN * 8;
+    constexpr int kPerR = ROPE ? (kPairs + kWsSplitThreads - 1) / kWsSplitThreads : 1;
+    float4 kcs0[kPerR], kcs1[kPerR];
+    auto load_kcs = [&](int jj) {
+      if constexpr (ROPE) {
+        const int kt = (t_begin + jj) * kBN;
+#pragma unroll
+        for (int i = 0; i < kPerR; ++i) {
+          const int f = st + i * kWsSplitThreads;
+          const int r = f >> 3, c = (f & 7) ^ (r & 7), pos = kt + r;
+          if (f < kPairs && pos < seq) {
+            const float4* t = reinterpret_cast<const float4*>(a.rope_cs + (static_cast<size_t>(pos) * 32 + 4 * c) * 2);
+            kcs0[i] = __ldg(t);  // (cos, sin) of i = 4c, 4c+1
+            kcs1[i] = __ldg(t + 1);  // and 4c+2, 4c+3
+          }
+        }
+      }
+    };
+    load_kcs(0);
     for (int j = 0; j < ntiles; ++j) {
       const int s3 = j % kLoStages, s4 = j & (kRawStages - 1);
       const uint32_t ph = static_cast<uint32_t>(j / kLoStages - 1) & 1u;  // phase of tile j-3's release
@@ -336,7 +414,35 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       float4* vr = reinterpret_cast<float4*>(&sm.raw[s4][1][0][0][0]);
       float4* kl = reinterpret_cast<float4*>(&sm.lo[s3][0][0][0][0]);
       float4* vl = reinterpret_cast<float4*>(&sm.lo[s3][1][0][0][0]);
-      {
+      if constexpr (ROPE) {
+        // Rotate K in place (it is the hi operand), then take its lo part.
+        // Element i of a key row sits in column half 0 and element i + 32 in
+        // half 1 at the same swizzled offset: float4 f of half 0 (row f / 8,
+        // stored chunk f % 8 = logical chunk (f % 8) ^ (row % 8)) pairs with
+        // float4 f of half 1.  Rows at or past valid_len stay as they are
+        // (masked keys).
+        const int kt = (t_begin + j) * kBN;
+#pragma unroll
+        for (int i = 0; i < kPerR; ++i) {
+          const int f = st + i * kWsSplitThreads;
+          if (f < kPairs) {
+            float4 x0 = kr[f], x1 = kr[f + kPairs];
+            const int r = f >> 3, pos = kt + r;
+            if (pos < valid) {
+              const float4 t0 = kcs0[i], t1 = kcs1[i];  // (cos, sin) of i = 4c .. 4c+3, c = (f % 8) ^ (r % 8)
+              ws_rot(x0.x, x1.x, t0.x, t0.y);
+              ws_rot(x0.y, x1.y, t0.z, t0.w);
+              ws_rot(x0.z, x1.z, t1.x, t1.y);
+              ws_rot(x0.w, x1.w, t1.z, t1.w);
+              kr[f] = x0;
+              kr[f + kPairs] = x1;
+            }
+            kl[f] = make_float4(tf32_lo(x0.x), tf32_lo(x0.y), tf32_lo(x0.z), tf32_lo(x0.w));
+            kl[f + kPairs] = make_float4(tf32_lo(x1.x), tf32_lo(x1.y), tf32_lo(x1.z), tf32_lo(x1.w));
+          }
+        }
+        if (j + 1 < ntiles) load_kcs(j + 1);
+      } else {
         float4 x[kPer];
 #pragma unroll
         for (int i = 0; i < kPer; ++i)

@@ -194,5 +194,9 @@ def test_automatic_kernel_choice(mask, block, expect_tc):
         assert kid in _lib.KERNEL_TILED64_VARIANTS.values()
     assert rb.kernel_for(_shape(heads=2, seq=1024, d=32), rb.AttnParams.new(mask, 1024, 32, block=block)) \
         == rb.KERNEL_ROWWISE
-    # the caller's packed layout runs the tuned tiled kernel
-    assert rb.kernel_for(shape, params, packed=True) in _lib.KERNEL_TILED64_VARIANTS.values()
+    # the caller's packed layout: the two-issuer tensor-core kernel where a tensor-core kernel is
+    # chosen (the persistent variant has no packed form), else the tuned tiled kernel
+    if expect_tc:
+        assert rb.kernel_for(shape, params, packed=True) == rb._lib.KERNEL_TC32_WS
+    else:
+        assert rb.kernel_for(shape, params, packed=True) in _lib.KERNEL_TILED64_VARIANTS.values()
