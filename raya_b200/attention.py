@@ -317,14 +317,19 @@ class Cuda(AttentionKernel):
         qkv is the packed projection [batch][seq][3][heads][64] and ctx the
         context [batch][seq][heads][64], both CUDA float32 tensors; with
         rope_theta, q and k get raya's rotary embedding (ops.rs:110-141)
-        first.  Asynchronous on ``stream``."""
+        first.  Asynchronous on ``stream``, except that uploading
+        ``params.valid_len`` (``valid_len`` None) waits for the call, as in
+        attend_device.  A caller's ``workspace`` must stay allocated until
+        the call has run; one allocated here is held for the stream by
+        torch's caching allocator."""
         import torch
 
         d = make_desc(shape, params)
         theta = float(rope_theta or 0.0)
         need = ctypes.c_size_t()
         _check(lib.raya_attn_packed_workspace(ctypes.byref(d), theta, ctypes.byref(need)))
-        if workspace is None and need.value:
+        own_workspace = workspace is None and need.value > 0
+        if own_workspace:
             workspace = torch.empty(need.value // 4, dtype=torch.float32, device=qkv.device)
         keep = valid_len
         if keep is None:
@@ -337,8 +342,10 @@ class Cuda(AttentionKernel):
         ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
         _check(lib.raya_attn_forward_packed(ctypes.byref(d), qkv.data_ptr(), ctx.data_ptr(), keep.data_ptr(),
                                             theta, ws_ptr, ws_bytes, stream))
-        if valid_len is None or workspace is not None:
-            _sync(stream)  # uploaded lengths / the caller's workspace stay valid until done
+        if own_workspace:  # not reused by the allocator before the work queued on `stream` has run
+            workspace.record_stream(torch.cuda.ExternalStream(stream, device=qkv.device))
+        if valid_len is None:  # keep the uploaded lengths alive until the kernel has run
+            _sync(stream)
 
 
 STAGE_NAMES = ("qk", "softmax", "pv", "k_wait", "v_wait", "refill", "tiles", "total")
