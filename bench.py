@@ -57,7 +57,11 @@ def parse():
                     help="run raya's local_attention bench shapes and write results/kernel-bench/*.json")
     ap.add_argument("--soak", type=float, default=1.0,
                     help="seconds of untimed steps, clock-sampled, right before the timed region")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.packed and args.kernel != 0:
+        ap.error("--kernel does not apply with --packed: the packed entry points choose their kernel "
+                 "(raya_attn_kernel_for with packed != 0)")
+    return args
 
 
 def host_threads() -> int:
