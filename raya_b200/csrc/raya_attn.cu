@@ -32,8 +32,8 @@ constexpr int kMaxDevices = 64;
 constexpr int kMaxHeadDim = 256;
 constexpr long long kMaxSeq = 1ll << 29;
 constexpr long long kDefaultTimeoutCycles = 1ll << 31;  // ~1 s at B200 clocks
-// Host-buffer call: chunks of at least kHostChunkBytes (inputs + output),
-// at most kMaxHostChunks, round-robin over kHostStreams streams.
+// Host-buffer call: chunks of at least kHostChunkBytes (inputs + output), at
+// most kMaxHostChunks, through three streams: copies in, kernels, copies out.
 constexpr int kHostStreams = 3;
 constexpr int64_t kMaxHostChunks = 16;
 constexpr int64_t kHostChunkBytes = 16ll << 20;
@@ -150,8 +150,10 @@ struct DeviceCtx {
   bool ready = false;
   int* status = nullptr;
   int sms = 0;
-  cudaStream_t streams[3] = {nullptr, nullptr, nullptr};  // host-buffer call pipeline
+  cudaStream_t streams[3] = {nullptr, nullptr, nullptr};  // host-buffer call: copies in, kernels, copies out
   cudaEvent_t valid_ready = nullptr;
+  cudaEvent_t chunk_in[kMaxHostChunks] = {};    // chunk c's inputs are on the device
+  cudaEvent_t chunk_done[kMaxHostChunks] = {};  // chunk c's output is written
   float* buf[4] = {nullptr, nullptr, nullptr, nullptr};  // q, k, v, out
   size_t cap = 0;                                        // floats per buffer
   int32_t* dvalid = nullptr;                             // valid length per slice
@@ -842,6 +844,11 @@ raya_attn_status raya_attn_forward_host(const raya_attn_desc* desc, const float*
     }
     e = cudaEventCreateWithFlags(&ctx->valid_ready, cudaEventDisableTiming);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+    for (int64_t c = 0; c < kMaxHostChunks; ++c) {
+      e = cudaEventCreateWithFlags(&ctx->chunk_in[c], cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->chunk_done[c], cudaEventDisableTiming);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+    }
   }
   if (ctx->cap < n) {
     for (auto& p : ctx->buf) {
@@ -875,8 +882,11 @@ raya_attn_status raya_attn_forward_host(const raya_attn_desc* desc, const float*
   e = cudaEventRecord(ctx->valid_ready, ctx->streams[0]);
   if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
 
-  // Pipeline over chunks of slices on kHostStreams streams: the copy engines
-  // move chunk c+1 in and chunk c-1 out while chunk c computes.
+  // Pipeline over chunks of slices: stream 0 copies every chunk in, back to
+  // back; stream 1 runs chunk c's kernel once its inputs are in; stream 2
+  // copies chunk c out once its kernel is done.  The host-to-device copy
+  // engine (the bound: 3/4 of the bytes) never waits for a kernel or an
+  // outgoing copy, which one stream per chunk made it do.
   const size_t slice = static_cast<size_t>(desc->seq) * desc->head_dim;
   const size_t bytes_total = 4 * n * sizeof(float);
   const int64_t nchunks = std::max<int64_t>(
@@ -885,22 +895,27 @@ raya_attn_status raya_attn_forward_host(const raya_attn_desc* desc, const float*
   for (int64_t c = 0; c < nchunks; ++c) {
     const int64_t bh0 = nbh * c / nchunks, bh1 = nbh * (c + 1) / nchunks;
     if (bh1 <= bh0) continue;
-    cudaStream_t s = ctx->streams[c % kHostStreams];
+    cudaStream_t s_in = ctx->streams[0], s_run = ctx->streams[1], s_out = ctx->streams[2];
     const size_t off = static_cast<size_t>(bh0) * slice;
     const size_t cnt = static_cast<size_t>(bh1 - bh0) * slice;
     for (int i = 0; i < 3; ++i) {
-      e = cudaMemcpyAsync(ctx->buf[i] + off, src[i] + off, cnt * sizeof(float), cudaMemcpyHostToDevice, s);
+      e = cudaMemcpyAsync(ctx->buf[i] + off, src[i] + off, cnt * sizeof(float), cudaMemcpyHostToDevice, s_in);
       if (e != cudaSuccess) return cuda_fail(e, "copy inputs to device");
     }
-    e = cudaStreamWaitEvent(s, ctx->valid_ready, 0);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
+    e = cudaEventRecord(ctx->chunk_in[c], s_in);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s_run, ctx->chunk_in[c], 0);
+    if (e == cudaSuccess && c == 0) e = cudaStreamWaitEvent(s_run, ctx->valid_ready, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "chunk events");
     raya_attn_desc sub = *desc;
     sub.batch = bh1 - bh0;
     sub.heads = 1;
     st = launch_on(ctx, &sub, ctx->buf[0] + off, ctx->buf[1] + off, ctx->buf[2] + off, ctx->buf[3] + off,
-                   ctx->dvalid + bh0, s, RAYA_KERNEL_AUTO);
+                   ctx->dvalid + bh0, s_run, RAYA_KERNEL_AUTO);
     if (st != RAYA_ATTN_OK) return st;
-    e = cudaMemcpyAsync(out + off, ctx->buf[3] + off, cnt * sizeof(float), cudaMemcpyDeviceToHost, s);
+    e = cudaEventRecord(ctx->chunk_done[c], s_run);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s_out, ctx->chunk_done[c], 0);
+    if (e != cudaSuccess) return cuda_fail(e, "chunk events");
+    e = cudaMemcpyAsync(out + off, ctx->buf[3] + off, cnt * sizeof(float), cudaMemcpyDeviceToHost, s_out);
     if (e != cudaSuccess) return cuda_fail(e, "copy out to host");
   }
   for (auto& sm : ctx->streams) {
