@@ -385,7 +385,10 @@ def run_b200(args) -> None:
             e2e_s = float(t[0])
         e2e = {"value": round(flops_all / w.layers / e2e_s / 1e9, 3), "unit": "GFLOP/s",
                "ms_per_step": round(e2e_s * 1e3, 3),
-               "h2d_bytes_per_step": 3 * n * 4 + w.batch * 4, "d2h_bytes_per_step": n * 4,
+               # q, k, v rows below valid_len (the call copies no padding rows) + one length per slice
+               "h2d_bytes_per_step": 3 * int(valid.astype(np.int64).sum()) * w.heads * w.head_dim * 4
+                                     + w.batch * w.heads * 4,
+               "d2h_bytes_per_step": n * 4,
                "api": "raya_attn_forward_host (AttentionKernel::attend contract), pinned host buffers"}
         # the host call must agree with the device call (bit for bit when both
         # run the same kernel; --kernel may pick another variant for the device)

@@ -154,7 +154,7 @@ struct DeviceCtx {
   bool ready = false;
   int* status = nullptr;
   int sms = 0;
-  cudaStream_t streams[3] = {nullptr, nullptr, nullptr};  // host-buffer call: copies in, kernels, copies out
+  cudaStream_t streams[kHostStreams] = {};  // host-buffer call: copies in, kernels, copies out
   cudaEvent_t valid_ready = nullptr;
   cudaEvent_t chunk_in[kMaxHostChunks] = {};    // chunk c's inputs are on the device
   cudaEvent_t chunk_done[kMaxHostChunks] = {};  // chunk c's output is written
@@ -909,9 +909,27 @@ raya_attn_status raya_attn_forward_host(const raya_attn_desc* desc, const float*
     cudaStream_t s_in = ctx->streams[0], s_run = ctx->streams[1], s_out = ctx->streams[2];
     const size_t off = static_cast<size_t>(bh0) * slice;
     const size_t cnt = static_cast<size_t>(bh1 - bh0) * slice;
-    for (int i = 0; i < 3; ++i) {
-      e = cudaMemcpyAsync(ctx->buf[i] + off, src[i] + off, cnt * sizeof(float), cudaMemcpyHostToDevice, s_in);
-      if (e != cudaSuccess) return cuda_fail(e, "copy inputs to device");
+    // Only the valid rows of each slice go in: no kernel reads q, k or v rows
+    // at or past valid_len (keys there are masked, V rows there are zeroed in
+    // shared memory, q rows there are read as zero), so whatever the staging
+    // buffers hold there does not reach the output.  One 2-D copy per run of
+    // slices with the same valid length (rows of `valid` * head_dim floats,
+    // pitch seq * head_dim).
+    for (int64_t r0 = bh0; r0 < bh1;) {
+      const int32_t vl = ctx->slice_valid[r0];
+      int64_t r1 = r0 + 1;
+      while (r1 < bh1 && ctx->slice_valid[r1] == vl) ++r1;
+      if (vl > 0) {
+        const size_t pitch = slice * sizeof(float);
+        const size_t width = static_cast<size_t>(vl) * desc->head_dim * sizeof(float);
+        const size_t o = static_cast<size_t>(r0) * slice;
+        for (int i = 0; i < 3; ++i) {
+          e = cudaMemcpy2DAsync(ctx->buf[i] + o, pitch, src[i] + o, pitch, width, static_cast<size_t>(r1 - r0),
+                                cudaMemcpyHostToDevice, s_in);
+          if (e != cudaSuccess) return cuda_fail(e, "copy inputs to device");
+        }
+      }
+      r0 = r1;
     }
     e = cudaEventRecord(ctx->chunk_in[c], s_in);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(s_run, ctx->chunk_in[c], 0);

@@ -237,6 +237,30 @@ def test_padding_values_never_reach_the_output(cuda_device, mask, kernel):
     padded_rows_exact_zero(got, p, valid)
 
 
+@pytest.mark.parametrize("mask", [dict(mask=oracle.MASK_BLOCK, block=64, halo=1), B3, W64,
+                                  dict(mask=oracle.MASK_FULL)], ids=["block64", "block3", "window64", "full"])
+def test_host_call_copies_only_valid_rows(cuda_device, mask):
+    """The host-buffer call copies only the rows below valid_len to the
+    device, so its staging buffers keep whatever an earlier call left past
+    them (NaN and Inf here).  The result must still equal the device call on
+    the same inputs, bit for bit, with padded rows +0.0."""
+    batch, heads, seq = 6, 3, 700
+    p = oracle.Problem(batch, heads, seq, 64, **mask)
+    q, k, v = oracle.qkv(p.numel, 97)
+    valid = [700, 433, 64, 0, 1, 699]
+    qn, kn, vn = (x.copy().reshape(batch, heads, seq, 64) for x in (q, k, v))
+    for b, vl in enumerate(valid):
+        qn[b, :, vl:] = np.nan
+        kn[b, :, vl:] = np.inf
+        vn[b, :, vl:] = np.nan
+    # an earlier call with every row valid leaves NaN/Inf in the staging rows past `valid`
+    cuda_host_run(p, qn.reshape(-1), kn.reshape(-1), vn.reshape(-1), valid=[seq] * batch)
+    got = cuda_host_run(p, q, k, v, valid=valid)
+    want = cuda_device_run(p, q, k, v, valid=valid)
+    assert np.array_equal(got, want)
+    padded_rows_exact_zero(got, p, valid)
+
+
 @pytest.mark.parametrize("mask", [B3, W64, dict(mask=oracle.MASK_FULL)], ids=["block3", "window64", "full"])
 @pytest.mark.parametrize("kernel", [rb._lib.KERNEL_TC32_STREAM, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_PIPE,
                                     rb.KERNEL_AUTO])
