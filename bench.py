@@ -43,7 +43,7 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", default="c2")
     ap.add_argument("--halo", type=int, default=1)
-    ap.add_argument("--kernel", type=int, default=0, help="0 auto, 1 tiled64, 2 rowwise, 32 tc32, 33 tc32_pipe, 34 tc32_ws, 36 tc32_stream (3xTF32 tensor cores)")
+    ap.add_argument("--kernel", type=int, default=0, help="0 auto, 1 tiled64, 2 rowwise, 32 tc32, 33 tc32_pipe, 34 tc32_ws, 36 tc32_stream, 37 tc32_ws two-tile (3xTF32 tensor cores)")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -266,7 +266,8 @@ def run_b200(args) -> None:
     # the kernel that runs: the automatic choice, or the one asked for
     chosen = rb.kernel_for(shape, params, packed=args.packed) if args.kernel == rb.KERNEL_AUTO else args.kernel
     tiled_ids = set(rb._lib.KERNEL_TILED64_VARIANTS.values()) | {rb.KERNEL_TILED64}
-    TENSOR_KERNELS = (rb.KERNEL_TC32, rb._lib.KERNEL_TC32_PIPE, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_STREAM)
+    TENSOR_KERNELS = (rb.KERNEL_TC32, rb._lib.KERNEL_TC32_PIPE, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_STREAM,
+                      rb._lib.KERNEL_TC32_WS2)
     stream = torch.cuda.current_stream(dev)
 
     # Live FFMA peak of this GPU (the roofline denominator: no FP32 figure is
@@ -429,6 +430,8 @@ def run_b200(args) -> None:
                   if chosen == rb._lib.KERNEL_TC32_PIPE else
                   "tc32_ws, two MMA-issuing warps, O in tensor memory, 3xTF32 tcgen05 (raya_b200/csrc/tc32_ws.cuh), "
                   "kernel id 34" if chosen == rb._lib.KERNEL_TC32_WS else
+                  "tc32_ws with two 128-row tiles per CTA (raya_b200/csrc/tc32_ws.cuh), kernel id 37"
+                  if chosen == rb._lib.KERNEL_TC32_WS2 else
                   "tc32_stream, one resident CTA per SM streaming its row tiles, 3xTF32 tcgen05 "
                   "(raya_b200/csrc/tc32_stream.cuh), kernel id 36" if chosen == rb._lib.KERNEL_TC32_STREAM else
                   f"tiled64 (raya_b200/csrc/tiled64.cuh), kernel id {chosen}",

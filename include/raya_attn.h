@@ -77,8 +77,10 @@ typedef enum {
                                halo 0 and block 128 or 256; the tensor-core kernel
                                RAYA_KERNEL_TC32_WS for Full, windows of half width >= 64,
                                other blocks >= 128 and block masks with a halo whose
-                               allowed keys fill >= half of a 128-row CTA's key span; else
-                               the tuned tiled kernel; other head_dims: rowwise */
+                               allowed keys fill >= half of a 128-row CTA's key span, in
+                               its two-tile form RAYA_KERNEL_TC32_WS2 for such blocks
+                               below 128 with >= 1024 128-row tiles; else the tuned tiled
+                               kernel; other head_dims: rowwise */
   RAYA_KERNEL_TILED64 = 1,  /* the tuned tiled variant for the mask and block (head_dim 64):
                                W4R16_P2 for block <= 64 and windows, W4R32_P2 for
                                block >= 128 and Full */
@@ -105,7 +107,11 @@ typedef enum {
   /* The same pipeline in one resident CTA per SM that walks its 128-row
    * tiles back to back: each tile's q copy, key-tile splits and first QK^T
    * overlap the previous tile's last key tiles and output store. */
-  RAYA_KERNEL_TC32_STREAM = 36
+  RAYA_KERNEL_TC32_STREAM = 36,
+  /* RAYA_KERNEL_TC32_WS with two 128-row tiles per CTA, one after the
+   * other, each run as a CTA of its own (sharing only the CTA's launch,
+   * tensor-memory allocation and valid_len loads). */
+  RAYA_KERNEL_TC32_WS2 = 37
 } raya_kernel_id;
 
 /* Argument checks of validate (attention.rs:128-170), extended to the batch

@@ -100,6 +100,7 @@ int tuned_tiled(const raya_attn_desc* d) {
 // 256 every 128-row CTA has only 2 or 4 key tiles, and the persistent
 // variant, which overlaps one row tile's set-up and output with the previous
 // one's, wins (1.2x and 1.1x; from 512 on, or at halo >= 1, it loses).
+constexpr long long kTwoTileMinTiles = 1024;
 int auto_kernel(const raya_attn_desc* d) {
   if (d->head_dim != 64) return RAYA_KERNEL_ROWWISE;
   if (d->mask == RAYA_MASK_FULL) return RAYA_KERNEL_TC32_WS;
@@ -111,15 +112,22 @@ int auto_kernel(const raya_attn_desc* d) {
   const long long spanned = (tc32::kBM + blk - 1) / blk + (tc32::kBM % blk != 0 ? 1 : 0);
   const long long span = ((spanned + 2 * halo) * blk + tc32::kBN - 1) / tc32::kBN * tc32::kBN;
   const long long allowed = (2 * halo + 1) * blk;
-  return 2 * allowed >= span ? RAYA_KERNEL_TC32_WS : tuned_tiled(d);
+  if (2 * allowed < span) return tuned_tiled(d);
+  // Short key ranges (blocks below 128) and many 128-row tiles (>= ~7 waves
+  // of 148 SMs): two tiles per CTA share its launch and set-up (c2, c3-b64,
+  // c4: +1.5-2.6%; with fewer tiles the halved CTA count costs more).
+  const long long tiles = d->batch * d->heads * ((d->seq + tc32::kBM - 1) / tc32::kBM);
+  return tiles >= kTwoTileMinTiles ? RAYA_KERNEL_TC32_WS2 : RAYA_KERNEL_TC32_WS;
 }
 
 // The packed entry points' kernel: the two-issuer tensor-core kernel with the
 // packed layout where the automatic choice is a tensor-core kernel (the
-// persistent variant has no packed form), else the tuned tiled kernel.
+// persistent and two-tile variants have no packed form), else the tuned tiled
+// kernel.
 int packed_kernel(const raya_attn_desc* d) {
   const int id = auto_kernel(d);
-  return id == RAYA_KERNEL_TC32_WS || id == RAYA_KERNEL_TC32_STREAM ? RAYA_KERNEL_TC32_WS : tuned_tiled(d);
+  return id == RAYA_KERNEL_TC32_WS || id == RAYA_KERNEL_TC32_WS2 || id == RAYA_KERNEL_TC32_STREAM ? RAYA_KERNEL_TC32_WS
+                                                                                                : tuned_tiled(d);
 }
 
 // Device status word: bit 0 = a bounded wait gave up.  One per device that
@@ -188,8 +196,8 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
     e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_pipe_fwd),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::pipe_smem_bytes()));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_pipe smem)");
-    for (auto fn : {tc32::tc32_ws_fwd<tiled64::kHeadMajor, false>, tc32::tc32_ws_fwd<tiled64::kPacked, false>,
-                    tc32::tc32_ws_fwd<tiled64::kPacked, true>}) {
+    for (auto fn : {tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 1>, tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 2>,
+                    tc32::tc32_ws_fwd<tiled64::kPacked, false, 1>, tc32::tc32_ws_fwd<tiled64::kPacked, true, 1>}) {
       e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(tc32::pipe_smem_bytes()));
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_ws smem)");
@@ -424,7 +432,7 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     if (st != RAYA_ATTN_OK) return st;
     tc32::tc32_fwd<<<static_cast<unsigned>(grid), tc32::kThreads, tc32::smem_bytes(), stream>>>(a, maps);
   } else if ((kernel_id == RAYA_KERNEL_TC32_PIPE || kernel_id == RAYA_KERNEL_TC32_WS ||
-              kernel_id == RAYA_KERNEL_TC32_STREAM) &&
+              kernel_id == RAYA_KERNEL_TC32_WS2 || kernel_id == RAYA_KERNEL_TC32_STREAM) &&
              !stage_cycles) {
     if (d->head_dim != 64)
       return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tensor-core kernel needs head_dim 64, got %lld",
@@ -449,8 +457,11 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
       tc32::tc32_stream_fwd<<<static_cast<unsigned>(resident), tc32::kWsThreads, tc32::stream_smem_bytes(),
                               stream>>>(a, maps);
     } else if (kernel_id == RAYA_KERNEL_TC32_WS)
-      tc32::tc32_ws_fwd<tiled64::kHeadMajor, false>
+      tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 1>
           <<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
+    else if (kernel_id == RAYA_KERNEL_TC32_WS2)  // two 128-row tiles per CTA
+      tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 2>
+          <<<static_cast<unsigned>((grid + 1) / 2), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
     else
       tc32::tc32_pipe_fwd<<<static_cast<unsigned>(grid), tc32::kPipeThreads, tc32::pipe_smem_bytes(), stream>>>(
           a, maps);
@@ -674,7 +685,7 @@ raya_attn_status launch_packed(DeviceCtx* ctx_dev, const raya_attn_desc* desc, c
                           static_cast<uint64_t>(desc->heads));
     if (st != RAYA_ATTN_OK) return st;
     maps.k = maps.q;  // the same [64 rows][32] boxes of the packed tensor
-    (rope ? tc32::tc32_ws_fwd<tiled64::kPacked, true> : tc32::tc32_ws_fwd<tiled64::kPacked, false>)
+    (rope ? tc32::tc32_ws_fwd<tiled64::kPacked, true, 1> : tc32::tc32_ws_fwd<tiled64::kPacked, false, 1>)
         <<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), s>>>(a, maps);
   } else {
     const int id = tuned_tiled(desc);

@@ -93,7 +93,11 @@ __device__ __forceinline__ void ws_rot(float& x, float& y, float c, float sn) {
 // [batch*seq][heads][64]: encoder.rs:34-92).  ROPE: q and k rotated first
 // (packed layout only), q rows by the softmax warps before they enter tensor
 // memory, K tiles by the split warps before their lo parts are taken.
-template <int LAYOUT, bool ROPE>
+// UNITS: 128-row tiles per CTA (blockIdx.x * UNITS + 0 .. UNITS-1), run one
+// after the other, each exactly as a CTA of its own (empty rings, barriers
+// set up again), so that only the CTA's launch, exit, tensor-memory
+// allocation and valid_len loads are shared between them.
+template <int LAYOUT, bool ROPE, int UNITS>
 __global__ void __launch_bounds__(kWsThreads, 1)
     tc32_ws_fwd(const __grid_constant__ AttnArgs a, const __grid_constant__ PipeMaps maps) {
   static_assert(!ROPE || LAYOUT == tiled64::kPacked, "the rotation is fused into the packed layout only");
@@ -102,15 +106,30 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   PipeSmem& sm = *reinterpret_cast<PipeSmem*>(smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr));
 
   const int tid = threadIdx.x, warp = tid >> 5;
-  // 32-bit index math (the host keeps the grid below 2^31 CTAs).
-  const unsigned bh32 = blockIdx.x / static_cast<unsigned>(a.row_tiles);
-  const int tile = static_cast<int>(blockIdx.x - bh32 * static_cast<unsigned>(a.row_tiles));
+  const int seq = a.seq;
+  // 32-bit index math (the host keeps batch * heads * row_tiles below 2^31).
+  const unsigned nunits = static_cast<unsigned>(a.batch) * static_cast<unsigned>(a.heads) *
+                          static_cast<unsigned>(a.row_tiles);
+  // A unit's valid_len, read one unit ahead (used after the barrier set-up).
+  auto load_valid = [&](unsigned unit) {
+    return unit >= nunits ? 0
+           : a.valid_len ? a.valid_len[unit / static_cast<unsigned>(a.row_tiles) / static_cast<unsigned>(a.heads)]
+                         : seq;
+  };
+  int valid_next = load_valid(blockIdx.x * UNITS);
+  bool tmem_held = false;  // (uniform) tensor memory allocated by an earlier unit of this CTA
+#pragma unroll 1
+  for (int uu = 0; uu < UNITS; ++uu) {
+  const unsigned unit = blockIdx.x * UNITS + uu;
+  if (unit >= nunits) break;
+  const int valid_raw = valid_next;
+  if (uu + 1 < UNITS) valid_next = load_valid(unit + 1);
+  const unsigned bh32 = unit / static_cast<unsigned>(a.row_tiles);
+  const int tile = static_cast<int>(unit - bh32 * static_cast<unsigned>(a.row_tiles));
   const unsigned b32 = bh32 / static_cast<unsigned>(a.heads);
   const long long bh = bh32;
   const int b = static_cast<int>(b32);
   const int head = static_cast<int>(bh32 - b32 * static_cast<unsigned>(a.heads));
-  const int seq = a.seq;
-  const int valid_raw = a.valid_len ? a.valid_len[b] : seq;  // used after the barrier set-up below
   const int r0 = tile * kBM;
   // First row of this slice in the loads' row coordinate, and the output
   // rows (head-major: the slice's rows; packed: this head's 64 columns of
@@ -156,16 +175,23 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int idx = tid; idx < rows * 16; idx += kWsThreads)
       st_stream(outp + static_cast<size_t>(r0 + (idx >> 4)) * out_stride + (idx & 15) * 4, zero);
-    return;
+    continue;
   }
 
-  if (warp == 10) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&sm.tmem_base)),
-                 "r"(kPipeTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  if (!tmem_held) {
+    if (warp == 10) {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_addr(&sm.tmem_base)),
+                   "r"(kPipeTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tmem_held = true;
   }
   if (tid == 0) {
+    // A later unit's copies land where the split warps' stores went (seen
+    // through the end-of-unit barrier): order those before the async proxy.
+    if (UNITS > 1 && uu > 0) fence_proxy_async_smem();
     // The first copies: the q tile (into lo stage 2, which the split warps
     // first write for key tile 2, after q_ready), then the K/V tiles of the
     // first four raw stages.
@@ -544,14 +570,22 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       commit(&sm.pv_done2[pb], static_cast<uint32_t>(j >> 1) & 1u);
       if (j + kLoStages < ntiles) commit(&sm.v_free[s3], static_cast<uint32_t>(j / kLoStages) & 1u);
     }
+    if constexpr (UNITS > 1) {
+      // The next unit sets the barriers up again: the one commit no other
+      // thread waits for (PV of tile ntiles-2) must have arrived first.
+      if (ok && ntiles >= 2)
+        mbar_wait_bounded(&sm.pv_done2[(ntiles - 2) & 1], static_cast<uint32_t>((ntiles - 2) >> 1) & 1u, abort_flag,
+                          a.status, a.timeout_cycles);
+    }
   }
   __syncwarp();
 
-  // Release tensor memory (every path); after a timeout first drain this
-  // CTA's copies and MMAs still in flight (bounded).
+  // End of the unit (every path); after a timeout first drain this CTA's
+  // copies and MMAs still in flight (bounded), and stop.
   tc_fence_before();
   __syncthreads();
-  if (*abort_flag) {
+  const bool aborted = *abort_flag != 0;
+  if (aborted) {
     const long long t0 = clock64();
     auto drain = [&](uint64_t* bar, uint32_t parity) {
       while (!mbar_try_wait(bar, parity) && clock64() - t0 < a.timeout_cycles) {
@@ -568,9 +602,12 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     if ((tid == kWsQkThread || tid == kWsPvThread) && last_commit) drain(last_commit, last_commit_parity);
   }
   __syncthreads();
-  if (warp == 10) {
+  if (aborted) break;
+  }  // units of this CTA
+  if (tmem_held && warp == 10) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPipeTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(sm.tmem_base), "r"(kPipeTmemCols)
+                 : "memory");
   }
 }
 

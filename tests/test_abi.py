@@ -162,6 +162,19 @@ def test_packed_call_validates_on_the_host():
                                              None) == _lib.ERR_UNSUPPORTED
 
 
+def test_two_tile_form_for_short_blocks_with_many_tiles():
+    """Blocks below 128 with a halo and >= 1024 128-row tiles (c2: 32 x 12 x 8) run the two-tile
+    form of the tensor-core kernel; with fewer tiles, blocks of 128 or the packed layout, the
+    one-tile form."""
+    params = rb.AttnParams.new(rb.Mask.block(1), [1024] * 32, 64, block=64)
+    assert rb.kernel_for(_shape(heads=12, seq=1024, d=64, batch=32), params) == rb._lib.KERNEL_TC32_WS2
+    assert rb.kernel_for(_shape(heads=12, seq=1024, d=64, batch=32), params, packed=True) == rb._lib.KERNEL_TC32_WS
+    small = rb.AttnParams.new(rb.Mask.block(1), [1024] * 2, 64, block=64)
+    assert rb.kernel_for(_shape(heads=12, seq=1024, d=64, batch=2), small) == rb._lib.KERNEL_TC32_WS
+    b128 = rb.AttnParams.new(rb.Mask.block(1), [1024] * 32, 64, block=128)
+    assert rb.kernel_for(_shape(heads=12, seq=1024, d=64, batch=32), b128) == rb._lib.KERNEL_TC32_WS
+
+
 @pytest.mark.parametrize("mask,block,expect_tc", [
     (rb.Mask.block(1), 128, True),    # Block3: every allowed key of a 128-row span
     (rb.Mask.block(0), 256, "stream"),  # halo 0, 2-4 key tiles per 128-row tile: the persistent kernel
