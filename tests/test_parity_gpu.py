@@ -240,15 +240,17 @@ def test_padding_values_never_reach_the_output(cuda_device, mask, kernel):
 
 @pytest.mark.parametrize("mask", [dict(mask=oracle.MASK_BLOCK, block=64, halo=1), B3, W64,
                                   dict(mask=oracle.MASK_FULL)], ids=["block64", "block3", "window64", "full"])
-def test_host_call_copies_only_valid_rows(cuda_device, mask):
+@pytest.mark.parametrize("valid", [[700, 433, 64, 0, 1, 699], [700, 690, 650, 700, 600, 699]],
+                         ids=["mostly-padding", "little-padding"])
+def test_host_call_copies_only_valid_rows(cuda_device, mask, valid):
     """The host-buffer call copies only the rows below valid_len to the
     device, so its staging buffers keep whatever an earlier call left past
     them (NaN and Inf here).  The result must still equal the device call on
-    the same inputs, bit for bit, with padded rows +0.0."""
+    the same inputs, bit for bit, with padded rows +0.0, for light and for
+    heavy padding."""
     batch, heads, seq = 6, 3, 700
     p = oracle.Problem(batch, heads, seq, 64, **mask)
     q, k, v = oracle.qkv(p.numel, 97)
-    valid = [700, 433, 64, 0, 1, 699]
     qn, kn, vn = (x.copy().reshape(batch, heads, seq, 64) for x in (q, k, v))
     for b, vl in enumerate(valid):
         qn[b, :, vl:] = np.nan
