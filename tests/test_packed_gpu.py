@@ -52,6 +52,24 @@ def test_packed_layout_matches_split_rope_attend_merge(cuda_device, case, theta)
         assert (c[b, vl:] == 0.0).all()
 
 
+@pytest.mark.parametrize("theta", [None, 10000.0], ids=["no-rope", "rope1e4"])
+@pytest.mark.parametrize("case", [0, 1, 3], ids=["block64", "block3", "window64"])
+def test_packed_layout_edge_valid_lengths(cuda_device, case, theta):
+    """A sequence with nothing valid, one with a single valid row and one a row
+    past a 128-row tile: exact zeros past valid_len, the oracle's values below."""
+    okw, mask, block = MASKS[case]
+    batch, seq, heads = 3, 300, 2
+    valid = [0, 1, 129]
+    qkv = oracle.rand_vec(batch * seq * 3 * heads * 64, 91 + case)
+    want = oracle.encoder_attend(qkv, batch, seq, heads, 64, okw["mask"], okw.get("block", 128),
+                                 okw.get("halo", 1), okw.get("window", 64), valid, theta)
+    got = _run_packed(qkv, batch, seq, heads, mask, block, valid, theta)
+    assert_close(got, want, f"packed edge theta={theta}")
+    c = got.reshape(batch, seq, heads * 64)
+    for b, vl in enumerate(valid):
+        assert (c[b, vl:] == 0.0).all() and not np.signbit(c[b, vl:]).any()
+
+
 def test_packed_layout_equals_the_head_major_call_bit_for_bit(cuda_device):
     """Without rotation the fused layout only changes addressing: the result is
     the head-major call's with the same kernel, transposed, bit for bit."""
