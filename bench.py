@@ -264,7 +264,8 @@ def run_b200(args) -> None:
     dvalid = torch.from_numpy(valid).to(dev)
     kern = rb.Cuda(rb.CudaConfig(device=local, kernel=args.kernel))
     # the kernel that runs: the automatic choice, or the one asked for
-    chosen = rb.kernel_for(shape, params, packed=args.packed) if args.kernel == rb.KERNEL_AUTO else args.kernel
+    chosen = (rb.kernel_for(shape, params, packed=args.packed, rope=args.rope_theta > 0)
+              if args.kernel == rb.KERNEL_AUTO else args.kernel)
     tiled_ids = set(rb._lib.KERNEL_TILED64_VARIANTS.values()) | {rb.KERNEL_TILED64}
     TENSOR_KERNELS = (rb.KERNEL_TC32, rb._lib.KERNEL_TC32_PIPE, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_STREAM,
                       rb._lib.KERNEL_TC32_WS2)

@@ -166,8 +166,10 @@ raya_attn_status raya_attn_forward_ex(const raya_attn_desc* desc, const float* q
  * cos/sin table, written by the call); it may be NULL otherwise.  head_dim
  * must be 64.  Asynchronous on `stream`; allocates nothing.  Kernel: the
  * two-issuer tensor-core kernel (RAYA_KERNEL_TC32_WS) with this layout
- * wherever RAYA_KERNEL_AUTO picks a tensor-core kernel, else the tuned tiled
- * kernel (raya_attn_kernel_for with packed != 0 names it). */
+ * wherever RAYA_KERNEL_AUTO picks a tensor-core kernel (its two-tile form
+ * RAYA_KERNEL_TC32_WS2 where that is the choice and there is no rotation),
+ * else the tuned tiled kernel (raya_attn_kernel_for with packed != 0 names
+ * it). */
 raya_attn_status raya_attn_forward_packed(const raya_attn_desc* desc, const float* qkv, float* ctx,
                                           const int32_t* valid_len, float rope_theta, void* workspace,
                                           size_t workspace_bytes, void* stream);
@@ -226,8 +228,9 @@ const char* raya_attn_last_error(void);
 
 /* The kernel that raya_attn_forward, raya_attn_forward_host and
  * raya_attn_forward_ex(RAYA_KERNEL_AUTO) launch for this descriptor, or with
- * packed != 0 the packed entry points (a raya_kernel_id, the tiled kernel
- * resolved to its tuned variant).  Host-only: no device work.  No counterpart
+ * packed != 0 the packed entry points, without the rotation (packed = 1) or
+ * with it (packed = 2) (a raya_kernel_id, the tiled kernel resolved to its
+ * tuned variant).  Host-only: no device work.  No counterpart
  * in the reference, whose caller picks the kernel type itself
  * (crates/raya-kernels/src/attention.rs:113-125). */
 raya_attn_status raya_attn_kernel_for(const raya_attn_desc* desc, int packed, int* kernel);

@@ -224,12 +224,13 @@ def work(shape: AttnShape, params: AttnParams) -> tuple[int, int]:
     return pairs.value, rows.value
 
 
-def kernel_for(shape: AttnShape, params: AttnParams, packed: bool = False) -> int:
+def kernel_for(shape: AttnShape, params: AttnParams, packed: bool = False, rope: bool = False) -> int:
     """The kernel id the automatic choice launches for this call, in the
-    head-major or (``packed``) the caller's packed layout (host-only)."""
+    head-major or (``packed``) the caller's packed layout, there with or
+    without the rotation (``rope``) (host-only)."""
     d = make_desc(shape, params)
     kid = ctypes.c_int()
-    _check(lib.raya_attn_kernel_for(ctypes.byref(d), int(packed), ctypes.byref(kid)))
+    _check(lib.raya_attn_kernel_for(ctypes.byref(d), (2 if rope else 1) if packed else 0, ctypes.byref(kid)))
     return kid.value
 
 

@@ -121,13 +121,16 @@ int auto_kernel(const raya_attn_desc* d) {
 }
 
 // The packed entry points' kernel: the two-issuer tensor-core kernel with the
-// packed layout where the automatic choice is a tensor-core kernel (the
-// persistent and two-tile variants have no packed form), else the tuned tiled
-// kernel.
-int packed_kernel(const raya_attn_desc* d) {
+// packed layout where the automatic choice is a tensor-core kernel, else the
+// tuned tiled kernel.  Its two-tile form where that is the choice, except with
+// the rotation (whose two-tile form spills registers and measured slower);
+// the persistent kernel has no packed form.
+int packed_kernel(const raya_attn_desc* d, bool rope) {
   const int id = auto_kernel(d);
-  return id == RAYA_KERNEL_TC32_WS || id == RAYA_KERNEL_TC32_WS2 || id == RAYA_KERNEL_TC32_STREAM ? RAYA_KERNEL_TC32_WS
-                                                                                                : tuned_tiled(d);
+  if (id == RAYA_KERNEL_TC32_WS2 && !rope) return id;
+  return id == RAYA_KERNEL_TC32_WS || id == RAYA_KERNEL_TC32_WS2 || id == RAYA_KERNEL_TC32_STREAM
+             ? RAYA_KERNEL_TC32_WS
+             : tuned_tiled(d);
 }
 
 // Device status word: bit 0 = a bounded wait gave up.  One per device that
@@ -197,7 +200,8 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::pipe_smem_bytes()));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_pipe smem)");
     for (auto fn : {tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 1>, tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 2>,
-                    tc32::tc32_ws_fwd<tiled64::kPacked, false, 1>, tc32::tc32_ws_fwd<tiled64::kPacked, true, 1>}) {
+                    tc32::tc32_ws_fwd<tiled64::kPacked, false, 1>, tc32::tc32_ws_fwd<tiled64::kPacked, true, 1>,
+                    tc32::tc32_ws_fwd<tiled64::kPacked, false, 2>}) {
       e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(tc32::pipe_smem_bytes()));
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_ws smem)");
@@ -668,7 +672,8 @@ raya_attn_status launch_packed(DeviceCtx* ctx_dev, const raya_attn_desc* desc, c
   a.rope_cs = rope_cs;
   const uint64_t rows = static_cast<uint64_t>(desc->batch) * desc->seq;
   raya_attn_status st;
-  if (packed_kernel(desc) == RAYA_KERNEL_TC32_WS) {
+  const int pk = packed_kernel(desc, rope);
+  if (pk == RAYA_KERNEL_TC32_WS || pk == RAYA_KERNEL_TC32_WS2) {
     a.row_tiles = static_cast<int>((desc->seq + tc32::kBM - 1) / tc32::kBM);
     const long long grid = static_cast<long long>(desc->batch) * desc->heads * a.row_tiles;
     if (grid > 0x7fffffffll)
@@ -685,8 +690,12 @@ raya_attn_status launch_packed(DeviceCtx* ctx_dev, const raya_attn_desc* desc, c
                           static_cast<uint64_t>(desc->heads));
     if (st != RAYA_ATTN_OK) return st;
     maps.k = maps.q;  // the same [64 rows][32] boxes of the packed tensor
-    (rope ? tc32::tc32_ws_fwd<tiled64::kPacked, true, 1> : tc32::tc32_ws_fwd<tiled64::kPacked, false, 1>)
-        <<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), s>>>(a, maps);
+    if (pk == RAYA_KERNEL_TC32_WS2)  // two 128-row tiles per CTA (no rotation)
+      tc32::tc32_ws_fwd<tiled64::kPacked, false, 2>
+          <<<static_cast<unsigned>((grid + 1) / 2), tc32::kWsThreads, tc32::pipe_smem_bytes(), s>>>(a, maps);
+    else
+      (rope ? tc32::tc32_ws_fwd<tiled64::kPacked, true, 1> : tc32::tc32_ws_fwd<tiled64::kPacked, false, 1>)
+          <<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), s>>>(a, maps);
   } else {
     const int id = tuned_tiled(desc);
     const PackedVariant* pv = nullptr;
@@ -977,7 +986,7 @@ raya_attn_status raya_attn_kernel_for(const raya_attn_desc* desc, int packed, in
   raya_attn_status st = check_shape(desc);
   if (st != RAYA_ATTN_OK) return st;
   if (!kernel) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null kernel pointer");
-  *kernel = packed ? packed_kernel(desc) : auto_kernel(desc);
+  *kernel = packed ? packed_kernel(desc, packed == 2) : auto_kernel(desc);
   return RAYA_ATTN_OK;
 }
 

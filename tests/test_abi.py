@@ -164,11 +164,14 @@ def test_packed_call_validates_on_the_host():
 
 def test_two_tile_form_for_short_blocks_with_many_tiles():
     """Blocks below 128 with a halo and >= 1024 128-row tiles (c2: 32 x 12 x 8) run the two-tile
-    form of the tensor-core kernel; with fewer tiles, blocks of 128 or the packed layout, the
-    one-tile form."""
+    form of the tensor-core kernel, in the packed layout too unless it rotates; with fewer tiles or
+    blocks of 128, the one-tile form."""
     params = rb.AttnParams.new(rb.Mask.block(1), [1024] * 32, 64, block=64)
-    assert rb.kernel_for(_shape(heads=12, seq=1024, d=64, batch=32), params) == rb._lib.KERNEL_TC32_WS2
-    assert rb.kernel_for(_shape(heads=12, seq=1024, d=64, batch=32), params, packed=True) == rb._lib.KERNEL_TC32_WS
+    c2 = _shape(heads=12, seq=1024, d=64, batch=32)
+    assert rb.kernel_for(c2, params) == rb._lib.KERNEL_TC32_WS2
+    assert rb.kernel_for(c2, params, packed=True) == rb._lib.KERNEL_TC32_WS2
+    assert rb.kernel_for(c2, params, packed=True, rope=True) == rb._lib.KERNEL_TC32_WS
+    assert rb.kernel_for(c2, params, rope=True) == rb._lib.KERNEL_TC32_WS2  # head-major: no rotation
     small = rb.AttnParams.new(rb.Mask.block(1), [1024] * 2, 64, block=64)
     assert rb.kernel_for(_shape(heads=12, seq=1024, d=64, batch=2), small) == rb._lib.KERNEL_TC32_WS
     b128 = rb.AttnParams.new(rb.Mask.block(1), [1024] * 32, 64, block=128)
@@ -209,7 +212,8 @@ def test_automatic_kernel_choice(mask, block, expect_tc):
         == rb.KERNEL_ROWWISE
     # the caller's packed layout: the two-issuer tensor-core kernel where a tensor-core kernel is
     # chosen (the persistent variant has no packed form), else the tuned tiled kernel
-    if expect_tc:
-        assert rb.kernel_for(shape, params, packed=True) == rb._lib.KERNEL_TC32_WS
-    else:
-        assert rb.kernel_for(shape, params, packed=True) in _lib.KERNEL_TILED64_VARIANTS.values()
+    for rope in (False, True):
+        if expect_tc:
+            assert rb.kernel_for(shape, params, packed=True, rope=rope) == rb._lib.KERNEL_TC32_WS
+        else:
+            assert rb.kernel_for(shape, params, packed=True, rope=rope) in _lib.KERNEL_TILED64_VARIANTS.values()

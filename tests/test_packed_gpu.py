@@ -70,13 +70,18 @@ def test_packed_layout_edge_valid_lengths(cuda_device, case, theta):
         assert (c[b, vl:] == 0.0).all() and not np.signbit(c[b, vl:]).any()
 
 
-def test_packed_layout_equals_the_head_major_call_bit_for_bit(cuda_device):
+# (batch, seq, heads, valid): 48 row tiles (one tile per CTA), and 1024 row
+# tiles at block 64 (two tiles per CTA, the form the automatic choice takes).
+BIG = (8, 512, 32, [512, 300, 257, 256, 511, 129, 0, 400])
+
+
+@pytest.mark.parametrize("dims", [(2, 1000, 3, [1000, 511]), BIG], ids=["48-tiles", "1024-tiles"])
+def test_packed_layout_equals_the_head_major_call_bit_for_bit(cuda_device, dims):
     """Without rotation the fused layout only changes addressing: the result is
     the head-major call's with the same kernel, transposed, bit for bit."""
     import torch
 
-    batch, seq, heads = 2, 1000, 3
-    valid = [1000, 511]
+    batch, seq, heads, valid = dims
     qkv = oracle.rand_vec(batch * seq * 3 * heads * 64, 9)
     got = _run_packed(qkv, batch, seq, heads, rb.Mask.block(1), 64, valid, None)
     x = qkv.reshape(batch, seq, 3, heads, 64)
@@ -90,6 +95,23 @@ def test_packed_layout_equals_the_head_major_call_bit_for_bit(cuda_device):
     rb.sync_status()
     head_major = out.cpu().numpy().reshape(batch, heads, seq, 64).transpose(0, 2, 1, 3).reshape(-1)
     assert np.array_equal(got, head_major)
+
+
+@pytest.mark.parametrize("theta", [None, 10000.0], ids=["no-rope", "rope1e4"])
+def test_packed_layout_with_many_row_tiles_matches_the_oracle(cuda_device, theta):
+    """Enough row tiles for two per CTA (the form taken without rotation; with
+    it, one per CTA), ragged and empty sequences among them."""
+    batch, seq, heads, valid = BIG
+    assert rb.kernel_for(rb.AttnShape(heads=heads, seq=seq, head_dim=64, batch=batch),
+                         rb.AttnParams.new(rb.Mask.block(1), valid, 64, block=64), packed=True,
+                         rope=theta is not None) == (rb._lib.KERNEL_TC32_WS2 if theta is None else rb._lib.KERNEL_TC32_WS)
+    qkv = oracle.rand_vec(batch * seq * 3 * heads * 64, 13)
+    want = oracle.encoder_attend(qkv, batch, seq, heads, 64, oracle.MASK_BLOCK, 64, 1, 64, valid, theta)
+    got = _run_packed(qkv, batch, seq, heads, rb.Mask.block(1), 64, valid, theta)
+    assert_close(got, want, f"packed two tiles theta={theta}")
+    c = got.reshape(batch, seq, heads * 64)
+    for b, vl in enumerate(valid):
+        assert (c[b, vl:] == 0.0).all() and not np.signbit(c[b, vl:]).any()
 
 
 def test_long_positions_rotate_like_the_reference(cuda_device):
