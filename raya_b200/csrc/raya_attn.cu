@@ -200,6 +200,7 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::pipe_smem_bytes()));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_pipe smem)");
     for (auto fn : {tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 1>, tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 2>,
+                    tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 4>,
                     tc32::tc32_ws_fwd<tiled64::kPacked, false, 1>, tc32::tc32_ws_fwd<tiled64::kPacked, true, 1>,
                     tc32::tc32_ws_fwd<tiled64::kPacked, false, 2>}) {
       e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -463,6 +464,9 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     } else if (kernel_id == RAYA_KERNEL_TC32_WS)
       tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 1>
           <<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
+    else if (kernel_id == RAYA_KERNEL_TC32_WS2 && a.row_tiles == 4)  // a whole slice of four row tiles per CTA
+      tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 4>
+          <<<static_cast<unsigned>((grid + 3) / 4), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
     else if (kernel_id == RAYA_KERNEL_TC32_WS2)  // two 128-row tiles per CTA
       tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 2>
           <<<static_cast<unsigned>((grid + 1) / 2), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);

@@ -268,16 +268,18 @@ def test_host_call_copies_only_valid_rows(cuda_device, mask, valid):
 @pytest.mark.parametrize("kernel", [rb._lib.KERNEL_TC32_WS2, rb._lib.KERNEL_TC32_STREAM, rb._lib.KERNEL_TC32_WS,
                                     rb._lib.KERNEL_TC32_PIPE,
                                     rb.KERNEL_AUTO])
-def test_many_units_per_sm(cuda_device, mask, kernel):
+@pytest.mark.parametrize("seq", [700, 512], ids=["seq700", "seq512"])
+def test_many_units_per_sm(cuda_device, mask, kernel, seq):
     """More (slice, 128-row) units than SMs, so several CTAs run on each SM
     in turn, with padding-only units (valid 0 and short sequences) and ragged
-    tails."""
+    tails.  At seq 512 a slice is four row tiles (kernel 37 then runs four
+    per CTA)."""
     rng = np.random.default_rng(123)
     batch = 48 if mask is not W64 else 40
-    p = oracle.Problem(batch, 4, 700, 64, **mask)
+    p = oracle.Problem(batch, 4, seq, 64, **mask)
     q, k, v = oracle.qkv(p.numel, 4242)
-    valid = [int(x) for x in rng.integers(0, 701, size=batch)]
-    valid[:4] = [0, 1, 700, 129]
+    valid = [int(x) for x in rng.integers(0, seq + 1, size=batch)]
+    valid[:4] = [0, 1, seq, 129]
     want = oracle.naive(p, q, k, v, valid)
     got = cuda_device_run(p, q, k, v, valid=valid, kernel=kernel)
     assert_close(got, want, f"kernel {kernel}")
