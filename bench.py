@@ -431,7 +431,8 @@ def run_b200(args) -> None:
                   if chosen == rb._lib.KERNEL_TC32_PIPE else
                   "tc32_ws, two MMA-issuing warps, O in tensor memory, 3xTF32 tcgen05 (raya_b200/csrc/tc32_ws.cuh), "
                   "kernel id 34" if chosen == rb._lib.KERNEL_TC32_WS else
-                  "tc32_ws with two 128-row tiles per CTA (raya_b200/csrc/tc32_ws.cuh), kernel id 37"
+                  ("tc32_ws with four 128-row tiles (a whole slice) per CTA" if (shape.seq + 127) // 128 == 4 and not args.packed
+                   else "tc32_ws with two 128-row tiles per CTA") + " (raya_b200/csrc/tc32_ws.cuh), kernel id 37"
                   if chosen == rb._lib.KERNEL_TC32_WS2 else
                   "tc32_stream, one resident CTA per SM streaming its row tiles, 3xTF32 tcgen05 "
                   "(raya_b200/csrc/tc32_stream.cuh), kernel id 36" if chosen == rb._lib.KERNEL_TC32_STREAM else

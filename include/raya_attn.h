@@ -108,9 +108,11 @@ typedef enum {
    * tiles back to back: each tile's q copy, key-tile splits and first QK^T
    * overlap the previous tile's last key tiles and output store. */
   RAYA_KERNEL_TC32_STREAM = 36,
-  /* RAYA_KERNEL_TC32_WS with two 128-row tiles per CTA, one after the
-   * other, each run as a CTA of its own (sharing only the CTA's launch,
-   * tensor-memory allocation and valid_len loads). */
+  /* RAYA_KERNEL_TC32_WS with two 128-row tiles per CTA (four where a
+   * (batch, head) slice is four row tiles, seq 385..512, so that a CTA runs
+   * the whole slice; head-major layout), one after the other, each run as a
+   * CTA of its own (sharing only the CTA's launch, tensor-memory allocation
+   * and valid_len loads). */
   RAYA_KERNEL_TC32_WS2 = 37
 } raya_kernel_id;
 

@@ -122,8 +122,9 @@ int auto_kernel(const raya_attn_desc* d) {
 
 // The packed entry points' kernel: the two-issuer tensor-core kernel with the
 // packed layout where the automatic choice is a tensor-core kernel, else the
-// tuned tiled kernel.  Its two-tile form where that is the choice, except with
-// the rotation (whose two-tile form spills registers and measured slower);
+// tuned tiled kernel.  Its two-tile form where that is the choice (two tiles
+// per CTA in this layout), except with the rotation (whose two-tile form
+// spills registers and measured slower);
 // the persistent kernel has no packed form.
 int packed_kernel(const raya_attn_desc* d, bool rope) {
   const int id = auto_kernel(d);
