@@ -1,19 +1,26 @@
 #!/usr/bin/env python
 """Benchmark of the B200 block-local attention path (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2] [--halo 1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c5] [--halo 1]
     python bench.py --impl reference ...      # the reference's CPU algorithm
 
 A step is one forward pass of block-local attention over one batch of the
-workload (default c2: batch 32, 12 heads, seq 1024, head_dim 64, block 64,
-Block3 = halo 1, valid lengths U[512, 1024], N(0,1) inputs from seed 1).
-Under torchrun every rank owns its own batch of 32 sequences of a global
-batch of 32*N (batch x heads is the shard; no collective on the data path):
-weak scaling.  `value` is whole-job algorithmic GFLOP/s (4 * head_dim FLOPs
-per allowed query/key pair, counted exactly), timed with CUDA events over K
-steps, max over ranks.  `e2e` is the same metric through the host-buffer API
-(raya_attn_forward_host: pinned host inputs -> device -> kernel -> host
-output, synchronous), wall-clock, max over ranks.
+workload.  The default is c5, the configuration the headline metric is
+quoted on: batch 256, 16 heads, seq 8192, head_dim 64, block 128, Block3 =
+halo 1, valid lengths U[4096, 8192], N(0,1) inputs from seed 4 (34.4 GB of
+q, k, v and out, generated on the device).
+
+Under torchrun (N ranks, one per GPU) the workload's batch x heads slices are
+split over the ranks by raya_attn_shard, balanced by allowed pairs, and each
+rank generates and runs only its own slices (strong scaling; no collective
+in the timed region).  `value` is whole-job algorithmic GFLOP/s (4 * head_dim
+FLOPs per allowed query/key pair, counted exactly), timed with CUDA events
+over K steps, max over ranks.  `gather` times, separately, the output gather
+to rank 0 over NVLink and checks it bit for bit.  `e2e` is the same metric
+through the host-buffer API (raya_attn_forward_host: pinned host inputs ->
+device -> kernel -> host output, synchronous), every rank on its own slices,
+wall clock, max over ranks.  `--scaling weak` gives every rank a whole batch
+of the workload instead.
 """
 from __future__ import annotations
 
@@ -41,10 +48,15 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", default="c2")
+    ap.add_argument("--workload", default="c5")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="strong: the workload's slices split over the ranks; weak: a whole batch per rank")
+    ap.add_argument("--no-gather", action="store_true", help="skip the timed output gather to rank 0 (N > 1)")
+    ap.add_argument("--gather-reps", type=int, default=3)
     ap.add_argument("--halo", type=int, default=1)
-    ap.add_argument("--kernel", type=int, default=0, help="0 auto, 1 tiled64, 2 rowwise, 32 tc32, 33 tc32_pipe, 34 tc32_ws, 36 tc32_stream, 37 tc32_ws two-tile (3xTF32 tensor cores)")
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--kernel", type=int, default=0, help="0 auto, 1 tiled64, 2 rowwise, 34 tc32_ws, 36 tc32_stream, 37 tc32_ws two-tile (3xTF32 tensor cores)")
+    ap.add_argument("--e2e-steps", type=int, default=3,
+                    help="timed host-buffer calls (each copies the step's inputs in and its output out)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
@@ -203,9 +215,9 @@ def run_reference(args) -> None:
     line = {
         "metric": "block-local attn GFLOP/s", "value": round(gflops, 3), "unit": "GFLOP/s",
         "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(w, world),
+        "config": workload_config(w, world, args.scaling),
         "queries_per_s": round(rows / dt, 1),
         "cpu_baseline": {"value": round(gflops, 3), "unit": "GFLOP/s", "cores": threads,
                          "kind": "port", "sample": sample, "cpu": cpu_model(),
@@ -216,23 +228,53 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def workload_config(w, world: int) -> dict:
-    return {"workload": f"{w.name}: batch {w.batch}/GPU x {w.heads} heads x seq {w.seq} x d {w.head_dim},"
+def workload_config(w, world: int, scaling: str) -> dict:
+    strong = scaling == "strong"
+    gb = w.batch if strong else w.batch * world
+    per = "" if strong else "/GPU"
+    return {"workload": f"{w.name}: batch {w.batch}{per} x {w.heads} heads x seq {w.seq} x d {w.head_dim},"
                         f" block {w.block}, halo {w.halo} ({'Block3' if w.halo == 1 else 'own block'}),"
-                        f" valid {w.valid or 'full'}, seed {w.seed}, N(0,{w.stddev}^2)",
-            "global_batch": w.batch * world, "seq_len": w.seq, "heads": w.heads,
+                        f" valid {w.valid or 'full'}, seed {w.seed}, N(0,{w.stddev}^2)"
+                        + (f", {w.layers} layers" if w.layers > 1 else ""),
+            "global_batch": gb, "seq_len": w.seq, "heads": w.heads,
             "head_dim": w.head_dim, "block": w.block, "halo": w.halo,
-            "parallelism": f"batch x heads sharded over {world} GPU(s), no collective",
-            "l2": f"inputs+output {4 * w.numel * 4 / 2**20:.0f} MiB per GPU > 126 MiB L2 (no flush)"}
+            "parallelism": (f"batch x heads slices split over {world} GPU(s) by allowed pairs "
+                            "(raya_attn_shard), no collective in the timed region" if strong else
+                            f"a whole batch per GPU on {world} GPU(s), no collective"),
+            "l2": l2_note(4 * w.numel * 4 / (world if strong else 1))}
+
+
+def l2_note(nbytes: float) -> str:
+    mib = nbytes / 2**20
+    if nbytes > L2_BYTES:
+        return f"inputs+output {mib:.0f} MiB per GPU > 126 MiB L2 (no flush needed)"
+    return f"inputs+output {mib:.0f} MiB per GPU fit in the 126 MiB L2 (not flushed: L2-resident between steps)"
 
 
 # ---------------------------------------------------------------- B200 arm
+
+def kernel_label(rb, chosen, shape, packed) -> str:
+    if chosen == rb.KERNEL_ROWWISE:
+        return "rowwise (raya_b200/csrc/rowwise.cuh)"
+    if chosen == rb.KERNEL_TC32_WS:
+        return ("tc32_ws, two MMA-issuing warps, O in tensor memory, 3xTF32 tcgen05 (raya_b200/csrc/tc32_ws.cuh), "
+                "kernel id 34")
+    if chosen == rb.KERNEL_TC32_WS2:
+        return (("tc32_ws with four 128-row tiles (a whole slice) per CTA" if (shape.seq + 127) // 128 == 4
+                 and not packed else "tc32_ws with two 128-row tiles per CTA")
+                + " (raya_b200/csrc/tc32_ws.cuh), kernel id 37")
+    if chosen == rb.KERNEL_TC32_STREAM:
+        return ("tc32_stream, one resident CTA per SM streaming its row tiles, 3xTF32 tcgen05 "
+                "(raya_b200/csrc/tc32_stream.cuh), kernel id 36")
+    return f"tiled64 (raya_b200/csrc/tiled64.cuh), kernel id {chosen}"
+
 
 def run_b200(args) -> None:
     import torch
     import torch.distributed as dist
 
     import raya_b200 as rb
+    from raya_b200 import shards
     from raya_b200.workloads import CONFIGS, fill_device
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -246,45 +288,70 @@ def run_b200(args) -> None:
 
     w = CONFIGS[args.workload].with_halo(args.halo)
     D = w.head_dim
-    # This rank's batch entries: [rank*B, (rank+1)*B) of the global batch.
-    b0 = rank * w.batch
-    valid = w.valid_len(first=b0)
-    shape = rb.AttnShape(heads=w.heads, seq=w.seq, head_dim=D, batch=w.batch)
-    params = rb.AttnParams.new(rb.Mask.block(w.halo), valid, D, block=w.block)
-    pairs, rows = rb.work(shape, params)
-    n = w.numel
+    strong = args.scaling == "strong"
+    # The global problem and this rank's part of it.  Strong scaling: the
+    # workload's batch x heads slices are split over the ranks by
+    # raya_attn_shard (balanced by allowed pairs), each rank generating only
+    # its own slices (inputs are a function of the global element index).
+    # Weak scaling: every rank runs a whole batch of the workload (entries
+    # rank*batch ..), as independent problems.
+    gbatch = w.batch if strong else w.batch * world
+    gvalid = w.valid_len(first=0, count=gbatch)
+    gshape = rb.AttnShape(heads=w.heads, seq=w.seq, head_dim=D, batch=gbatch)
+    gparams = rb.AttnParams.new(rb.Mask.block(w.halo), gvalid, D, block=w.block)
+    sp = shards.plan(gshape, gparams, world) if strong else None
+    if strong:
+        bh0, bh1 = sp.range(rank)
+        shape, params = shards.shard_problem(gshape, gparams, bh0, bh1)
+        valid = np.asarray(params.valid_len, dtype=np.int32)
+    else:
+        bh0, bh1 = rank * w.batch * w.heads, (rank + 1) * w.batch * w.heads
+        valid = gvalid[rank * w.batch:(rank + 1) * w.batch]
+        shape = rb.AttnShape(heads=w.heads, seq=w.seq, head_dim=D, batch=w.batch)
+        params = rb.AttnParams.new(rb.Mask.block(w.halo), valid, D, block=w.block)
+    pairs, rows = rb.work(shape, params) if shape.batch > 0 else (0, 0)
+    slice_elems = w.seq * D
+    n = (bh1 - bh0) * slice_elems
+    gather_on = strong and world > 1 and not args.no_gather
     # One (q, k, v, out) set per encoder layer (c4 has 12; the others 1).
+    # Rank 0 of a gathered run owns the whole output tensor of layer 0 and
+    # writes its own slices straight into it.
     layers = []
     for layer in range(w.layers):
-        t = tuple(torch.empty(n, dtype=torch.float32, device=dev) for _ in range(4))
-        fill_device(w, t[:3], layer=layer, bh0=b0 * w.heads)
-        layers.append(t)
+        t = [torch.empty(max(n, 1), dtype=torch.float32, device=dev) for _ in range(3)]
+        fill_device(w, t, layer=layer, bh0=bh0)
+        if gather_on and rank == 0 and layer == 0:
+            full = torch.empty(sp.ranges[-1][1] * slice_elems, dtype=torch.float32, device=dev)
+            t.append(full[bh0 * slice_elems:bh1 * slice_elems])
+        else:
+            t.append(torch.empty(max(n, 1), dtype=torch.float32, device=dev))
+        layers.append(tuple(t))
     q, k, v, out = layers[0]
     pairs, rows = pairs * w.layers, rows * w.layers
-    dvalid = torch.from_numpy(valid).to(dev)
+    dvalid = torch.from_numpy(valid).to(dev) if shape.batch > 0 else None
     kern = rb.Cuda(rb.CudaConfig(device=local, kernel=args.kernel))
-    # the kernel that runs: the automatic choice, or the one asked for
     chosen = (rb.kernel_for(shape, params, packed=args.packed, rope=args.rope_theta > 0)
-              if args.kernel == rb.KERNEL_AUTO else args.kernel)
+              if args.kernel == rb.KERNEL_AUTO else args.kernel) if shape.batch > 0 else rb.KERNEL_AUTO
     tiled_ids = set(rb._lib.KERNEL_TILED64_VARIANTS.values()) | {rb.KERNEL_TILED64}
-    TENSOR_KERNELS = (rb.KERNEL_TC32, rb._lib.KERNEL_TC32_PIPE, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_STREAM,
-                      rb._lib.KERNEL_TC32_WS2)
+    TENSOR_KERNELS = (rb.KERNEL_TC32_WS, rb.KERNEL_TC32_STREAM, rb.KERNEL_TC32_WS2)
     stream = torch.cuda.current_stream(dev)
 
-    # Live FFMA peak of this GPU (the roofline denominator: no FP32 figure is
-    # in MEASURED_PEAKS.json), measured before the timed region.
+    # Live FFMA peak of this GPU (the fp32-equivalent denominator: no FP32
+    # figure is in MEASURED_PEAKS.json), measured before the timed region.
     ffma_tflops = rb.ffma_peak(5)
 
     if args.packed:
         # The same numbers laid out as the encoder's packed projection.
         packed = []
         for lq, lk, lv, lo in layers:
-            qkv = torch.stack([t.view(w.batch, w.heads, w.seq, D).transpose(1, 2) for t in (lq, lk, lv)],
+            qkv = torch.stack([t.view(shape.batch, shape.heads, w.seq, D).transpose(1, 2) for t in (lq, lk, lv)],
                               dim=2).contiguous().view(-1)
             packed.append((qkv, torch.empty_like(lo)))
         ws = torch.empty(w.seq * 64, dtype=torch.float32, device=dev) if args.rope_theta > 0 else None
 
     def step():
+        if shape.batch == 0:
+            return
         if args.packed:
             for qkv, ctx in packed:
                 kern.attend_packed(shape, params, qkv, ctx, valid_len=dvalid, rope_theta=args.rope_theta or None,
@@ -308,11 +375,12 @@ def run_b200(args) -> None:
         sampler.start()
     t_soak = time.perf_counter()
     while time.perf_counter() - t_soak < args.soak:
-        for _ in range(10):
+        for _ in range(4):
             step()
         torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
+    torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     for _ in range(args.steps):
@@ -334,15 +402,45 @@ def run_b200(args) -> None:
     gflops = flops_all / (ms_max * 1e-3) / 1e9
     qps = rows_all / (ms_max * 1e-3)
 
+    # The output gather to rank 0 (strong scaling, N > 1), timed on its own:
+    # every rank's layer-0 output into rank 0's whole-output tensor over
+    # NVLink.  Then rank 0 checks that gathered slices of every other rank are
+    # bit-identical to the same slices run on its own GPU.
+    gather = None
+    if gather_on:
+        reps = max(1, args.gather_reps)
+        times = []
+        for _ in range(reps + 1):  # the first is a warm-up
+            dist.barrier()
+            torch.cuda.synchronize(dev)
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+            shards.gather_to_rank0(out, sp, rank, out=full if rank == 0 else None)
+            g1.record(stream)
+            torch.cuda.synchronize(dev)
+            times.append(g0.elapsed_time(g1))
+        gt = torch.tensor([statistics.median(times[1:])], dtype=torch.float64, device=dev)
+        dist.all_reduce(gt, op=dist.ReduceOp.MAX)
+        moved = 4 * (sp.ranges[-1][1] - sp.range(0)[1] + sp.range(0)[0]) * slice_elems
+        gather = {"ms": round(float(gt[0]), 3), "bytes_to_rank0": moved,
+                  "gbps_into_rank0": round(moved / (float(gt[0]) * 1e-3) / 1e9, 1),
+                  "how": "NCCL point-to-point receives straight into rank 0's output tensor "
+                         "(raya_b200.shards.gather_to_rank0), median of "
+                         f"{reps} after a warm-up, CUDA events, max over ranks; not in `value`"}
+        if rank == 0:
+            gather["check"] = gather_check(rb, w, gshape, gparams, sp, full, dev)
+
     # Roofline of the kernel (per launch on this rank; a step is w.layers launches).
     flops_launch = 4.0 * D * pairs / w.layers
-    bytes_launch = 4.0 * D * (3 * float(valid.sum()) + w.batch * w.seq) * w.heads
+    bytes_launch = 4.0 * D * (3 * float(valid.sum()) * (1 if strong else w.heads)
+                              + shape.batch * shape.heads * w.seq)
     launch_ms = ms / w.layers
     achieved_tf = flops_launch / (launch_ms * 1e-3) / 1e12
     peaks, peak_kind = load_peaks()
     hbm = peaks.get("hbm_gbs")
     tkey = (f"{w.name}-halo{w.halo}" + (f"-k{chosen}" if chosen in TENSOR_KERNELS else "")
             + ("-packed" if args.packed else ""))
+    traffic = load_traffic(tkey) if world == 1 else None
     hbm_obj = {"achieved": round(bytes_launch / (launch_ms * 1e-3) / 1e9, 1), "peak": hbm,
                "unit": "GB/s", "frac": round(bytes_launch / (launch_ms * 1e-3) / 1e9 / hbm, 4) if hbm else None,
                "peak_source": f"MEASURED_PEAKS.json hbm_gbs (of {peak_kind})" if peak_kind == "measured"
@@ -358,56 +456,32 @@ def run_b200(args) -> None:
                     "work": "3 TF32 products (hi*lo, lo*hi, hi*hi) x 4 * head_dim flops per allowed pair",
                     "fp32_equivalent": {"achieved": round(achieved_tf, 3), "ffma_peak": round(ffma_tflops, 3),
                                         "frac": round(achieved_tf / ffma_tflops, 4)},
-                    "traffic": load_traffic(tkey), "algorithmic_bytes": bytes_launch, "hbm": hbm_obj}
+                    "traffic": traffic, "algorithmic_bytes": bytes_launch, "hbm": hbm_obj}
     else:
         roofline = {"bound": "ffma", "achieved": round(achieved_tf, 3), "peak": round(ffma_tflops, 3),
                     "unit": "TFLOP/s", "frac": round(achieved_tf / ffma_tflops, 4),
                     "peak_source": "measured live: raya_attn_ffma_peak (FP32 FFMA probe, this GPU)",
                     "nominal_peak": round(148 * 128 * 2 * 1.965e9 / 1e12, 1),
-                    "traffic": load_traffic(tkey),
-                    "algorithmic_bytes": bytes_launch, "hbm": hbm_obj}
+                    "traffic": traffic, "algorithmic_bytes": bytes_launch, "hbm": hbm_obj}
+    if world > 1:
+        roofline["per"] = "rank 0's launches"
 
-    # End to end through the host-buffer API (pinned inputs, synchronous).
+    # End to end through the host-buffer API (pinned inputs, synchronous), on
+    # every rank's own slices at once; the max over ranks is the step time.
     e2e = None
     if not args.no_e2e and not args.packed:
-        hq, hk, hv, ho = (torch.empty(n, dtype=torch.float32).pin_memory() for _ in range(4))
-        for h, d in zip((hq, hk, hv), (q, k, v)):
-            h.copy_(d)
-        hq_np, hk_np, hv_np, ho_np = (x.numpy() for x in (hq, hk, hv, ho))
-        kern.attend(shape, params, hq_np, hk_np, hv_np, ho_np)  # warm-up (staging buffers)
-        if world > 1:
-            dist.barrier()
-        t0 = time.perf_counter()
-        for _ in range(args.e2e_steps):
-            kern.attend(shape, params, hq_np, hk_np, hv_np, ho_np)
-        e2e_s = (time.perf_counter() - t0) / args.e2e_steps
-        if world > 1:
-            t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_s = float(t[0])
-        e2e = {"value": round(flops_all / w.layers / e2e_s / 1e9, 3), "unit": "GFLOP/s",
-               "ms_per_step": round(e2e_s * 1e3, 3),
-               # q, k, v rows below valid_len (the call copies no padding rows) + one length per slice
-               "h2d_bytes_per_step": 3 * int(valid.astype(np.int64).sum()) * w.heads * w.head_dim * 4
-                                     + w.batch * w.heads * 4,
-               "d2h_bytes_per_step": n * 4,
-               "api": "raya_attn_forward_host (AttentionKernel::attend contract), pinned host buffers"}
-        # the host call must agree with the device call (bit for bit when both
-        # run the same kernel; --kernel may pick another variant for the device)
-        diff = float((ho - out.cpu()).abs().max())
-        assert diff < 1e-5 and (args.kernel != 0 or diff == 0.0), \
-            f"host-buffer call differs from the device call by {diff}"
+        e2e = run_e2e(args, rb, kern, shape, params, q, k, v, out, valid, w, world, dev, flops_all / w.layers)
 
     # Stage proportions of one extra, instrumented launch (the reference
     # bench's "stages" field, benches/local_attention.rs:127-130,155-157).
     stages = None
-    if chosen in tiled_ids and not args.packed:
+    if not args.packed and shape.batch > 0 and chosen in tiled_ids:
         st = rb.stage_times(shape, params, q, k, v, out, valid_len=dvalid, kernel=chosen)
         stages = {key: round(val, 2) for key, val in st.items() if key.endswith("pct")}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.packed:
-        cpu = cpu_baseline(args, w, q, k, v, valid, dev)
+        cpu = cpu_baseline(args, w, q, k, v, out, gvalid if strong else valid, dev)
 
     if world > 1:
         dist.barrier()
@@ -417,43 +491,101 @@ def run_b200(args) -> None:
     line = {
         "metric": "block-local attn GFLOP/s", "value": round(gflops, 3), "unit": "GFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
-        "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), device-generated)",
-        "config": workload_config(w, world),
+        "config": workload_config(w, world, args.scaling),
         "queries_per_s": round(qps, 1),
         "frac_fp32_peak": round(achieved_tf / ffma_tflops, 4),
         "gpu_launches": args.steps * w.layers,
         "layout": ("packed qkv -> context" + (f", rope theta {args.rope_theta:g}" if args.rope_theta else "")
                    if args.packed else "head-major q, k, v -> out"),
-        "kernel": "rowwise (raya_b200/csrc/rowwise.cuh)" if chosen == rb.KERNEL_ROWWISE else
-                  "tc32, 3xTF32 tcgen05 (raya_b200/csrc/tc32.cuh), kernel id 32" if chosen == rb.KERNEL_TC32 else
-                  "tc32_pipe, warp-specialised 3xTF32 tcgen05 (raya_b200/csrc/tc32_pipe.cuh), kernel id 33"
-                  if chosen == rb._lib.KERNEL_TC32_PIPE else
-                  "tc32_ws, two MMA-issuing warps, O in tensor memory, 3xTF32 tcgen05 (raya_b200/csrc/tc32_ws.cuh), "
-                  "kernel id 34" if chosen == rb._lib.KERNEL_TC32_WS else
-                  ("tc32_ws with four 128-row tiles (a whole slice) per CTA" if (shape.seq + 127) // 128 == 4 and not args.packed
-                   else "tc32_ws with two 128-row tiles per CTA") + " (raya_b200/csrc/tc32_ws.cuh), kernel id 37"
-                  if chosen == rb._lib.KERNEL_TC32_WS2 else
-                  "tc32_stream, one resident CTA per SM streaming its row tiles, 3xTF32 tcgen05 "
-                  "(raya_b200/csrc/tc32_stream.cuh), kernel id 36" if chosen == rb._lib.KERNEL_TC32_STREAM else
-                  f"tiled64 (raya_b200/csrc/tiled64.cuh), kernel id {chosen}",
+        "kernel": kernel_label(rb, chosen, shape, args.packed),
         "kernel_choice": "automatic (raya_attn_kernel_for)" if args.kernel == rb.KERNEL_AUTO else "--kernel",
-        "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "stages": stages,
+        "roofline": roofline, "e2e": e2e, "gather": gather, "cpu_baseline": cpu, "clocks": clocks,
+        "stages": stages,
     }
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline(args, w, q, k, v, valid, dev) -> dict:
-    """The oracle's Tiled+AVX2 restatement on the host cores over a bounded
-    sample (whole sequences) of the same device-generated inputs."""
+def gather_check(rb, w, gshape, gparams, sp, full, dev) -> dict:
+    """Rank 0: the first and last slice of every rank's range, regenerated
+    and run on rank 0's GPU as one call, must equal the gathered output bit
+    for bit (slices are independent, so sharding changes no rounding)."""
     import torch
 
+    from raya_b200 import shards
+
+    picks = sorted({x for b, e in sp.ranges if e > b for x in (b, e - 1)})
+    n = w.seq * w.head_dim
+    tq, tk, tv = (torch.empty(len(picks) * n, dtype=torch.float32, device=dev) for _ in range(3))
+    for i, bh in enumerate(picks):
+        for t, x in enumerate((tq, tk, tv)):
+            rb.fill_normal(x[i * n:(i + 1) * n], w.layer_seed(0), t, bh * n, w.stddev)
+    gv = gparams.valid_array(gshape.batch)
+    sv = np.array([gv[bh // w.heads] for bh in picks], dtype=np.int32)
+    sub_shape = rb.AttnShape(heads=1, seq=w.seq, head_dim=w.head_dim, batch=len(picks))
+    sub_params = rb.AttnParams(mask=gparams.mask, block=gparams.block, valid_len=sv, scale=gparams.scale)
+    o = torch.empty_like(tq)
+    rb.Cuda().attend_device(sub_shape, sub_params, tq, tk, tv, o, valid_len=torch.from_numpy(sv).to(dev))
+    rb.sync_status()
+    want = torch.cat([full[bh * n:(bh + 1) * n] for bh in picks])
+    same = bool(torch.equal(o, want))
+    assert same, "gathered slices differ from the same slices run on one GPU"
+    return {"slices": picks, "bit_exact": same}
+
+
+def run_e2e(args, rb, kern, shape, params, q, k, v, out, valid, w, world, dev, flops_step) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    n = shape.numel()
+    if n:
+        hq, hk, hv, ho = (torch.empty(n, dtype=torch.float32).pin_memory() for _ in range(4))
+        for h, d in zip((hq, hk, hv), (q, k, v)):
+            h.copy_(d[:n])
+        hq_np, hk_np, hv_np, ho_np = (x.numpy() for x in (hq, hk, hv, ho))
+        kern.attend(shape, params, hq_np, hk_np, hv_np, ho_np)  # warm-up (staging buffers)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps if n else 0):
+        kern.attend(shape, params, hq_np, hk_np, hv_np, ho_np)
+    e2e_s = (time.perf_counter() - t0) / args.e2e_steps
+    # q, k, v rows below valid_len (the call copies no padding rows) + one length per slice
+    h2d = 3 * int(valid.astype(np.int64).sum()) * (shape.heads * w.head_dim * 4) + shape.batch * shape.heads * 4
+    d2h = n * 4
+    if world > 1:
+        t = torch.tensor([e2e_s, float(h2d), float(d2h)], dtype=torch.float64, device=dev)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        e2e_s, h2d_all, d2h_all = float(mx[0]), float(t[1]), float(t[2])
+    else:
+        h2d_all, d2h_all = float(h2d), float(d2h)
+    if n:
+        # the host call must agree with the device call (bit for bit when both
+        # run the same kernel; --kernel may pick another variant for the device)
+        diff = float((ho - out[:n].cpu()).abs().max())
+        assert diff < 1e-5 and (args.kernel != 0 or diff == 0.0), \
+            f"host-buffer call differs from the device call by {diff}"
+    return {"value": round(flops_step / e2e_s / 1e9, 3), "unit": "GFLOP/s",
+            "ms_per_step": round(e2e_s * 1e3, 3),
+            "h2d_bytes_per_step": int(h2d_all), "d2h_bytes_per_step": int(d2h_all),
+            "h2d_gbps": round(h2d_all / e2e_s / 1e9, 1),
+            "steps": args.e2e_steps,
+            "api": "raya_attn_forward_host (AttentionKernel::attend contract), pinned host buffers, "
+                   "every rank its own slices, wall clock, max over ranks"}
+
+
+def cpu_baseline(args, w, q, k, v, out, valid, dev) -> dict:
+    """The oracle's Tiled+AVX2 restatement on the host cores over a bounded
+    sample (whole sequences) of the same device-generated inputs.  The
+    sample's CPU outputs are also compared with the GPU's outputs for the same
+    slices (max-abs 1e-5, the parity bar of the tests)."""
     import oracle
 
     threads = host_threads()
     D, L, H = w.head_dim, w.seq, w.heads
-    p_all = oracle.Problem(w.batch, H, L, D, mask=oracle.MASK_BLOCK, block=w.block, halo=w.halo)
-    pairs_all, _ = oracle.count(p_all, valid)
     # calibrate on one sequence, then size the sample to ~cpu_seconds
     host = {}
 
@@ -464,24 +596,27 @@ def cpu_baseline(args, w, q, k, v, valid, dev) -> dict:
             host.update(m=m, x=tuple(x[:m].cpu().numpy() for x in (q, k, v)))
         qs, ks, vs = host["x"]
         t0 = time.perf_counter()
-        oracle.tiled(ps, qs, ks, vs, valid[:nb], threads=threads)
+        o = oracle.tiled(ps, qs, ks, vs, valid[:nb], threads=threads)
         dt = time.perf_counter() - t0
         pairs, _ = oracle.count(ps, valid[:nb])
-        return 4 * D * pairs / dt / 1e9, dt
-    rate, dt1 = run(1)
+        return 4 * D * pairs / dt / 1e9, dt, o
+    rate, dt1, _ = run(1)
     nb = int(max(1, min(w.batch, args.cpu_seconds / max(dt1, 1e-3))))
-    rates, total, reps = [], 0.0, 0
+    rates, total, reps, o = [], 0.0, 0, None
     while total < args.cpu_seconds and reps < 200:
-        rate, dt = run(nb)
+        rate, dt, o = run(nb)
         rates.append(rate)
         total += dt
         reps += 1
     rate = statistics.median(rates)
+    m = nb * H * L * D
+    diff = float(np.abs(out[:m].cpu().numpy().astype(np.float64) - o.astype(np.float64)).max())
     return {"value": round(rate, 3), "unit": "GFLOP/s", "cores": threads, "kind": "port",
             "sample": f"{nb} of {w.batch} sequences x {H} heads of {w.name} (same inputs), "
                       f"median of {reps} passes, {total:.1f} s of CPU work",
             "cpu": cpu_model(),
-            "what": "C restatement of raya Tiled + AVX2 micro-kernels (oracle/tiled.c)"}
+            "what": "C restatement of raya Tiled + AVX2 micro-kernels (oracle/tiled.c)",
+            "parity": {"slices": nb * H, "max_abs_vs_gpu": diff, "within_1e-5": diff < 1e-5}}
 
 
 def raya_bench(args) -> None:

@@ -10,7 +10,8 @@
  *   validate                        crates/raya-kernels/src/attention.rs:128-170
  *   Tiled::attend                   crates/raya-kernels/src/tiled/mod.rs:138-149
  * A Rust maintainer binds `raya_attn_forward_host` with `batch = 1` inside an
- * `impl AttentionKernel for Cuda` (the binding is shown in INTEGRATION.md).
+ * `impl AttentionKernel for Cuda`; the FFI crate crates/raya-kernels-cuda of
+ * this repository is that binding.
  *
  * Layout contract (attention.rs:72-78, extended with a batch dimension):
  * q, k, v and out are row-major fp32 `[batch][heads][seq][head_dim]`; the
@@ -92,17 +93,13 @@ typedef enum {
   RAYA_KERNEL_TILED64_W4R16 = 19,
   RAYA_KERNEL_TILED64_W4R16_P2 = 20,
   RAYA_KERNEL_TILED64_W4R32_P2 = 21,
-  /* Tensor cores (tcgen05, kind::tf32) in 3xTF32: hi/lo split operands,
-   * fp32-level accuracy; head_dim 64, 128-row CTAs. */
-  RAYA_KERNEL_TC32 = 32,
-  /* The same arithmetic, warp-specialised and pipelined: q and p held in
-   * tensor memory, a split warpgroup preparing K/V operand stages, one MMA
-   * thread overlapping QK^T of the next key tile with this tile's softmax. */
-  RAYA_KERNEL_TC32_PIPE = 33,
-  /* The same, with QK^T and PV issued by two warps (one issuing thread
-   * sustains only ~2/3 of the tensor core's rate at N = 64) and the O
-   * accumulator in tensor memory, rescaled only when a row's max grows by
-   * more than 2^8. */
+  /* Tensor cores (tcgen05, kind::tf32) in 3xTF32: each fp32 operand enters
+   * as itself (read as TF32) and as its remainder, three products per tile,
+   * fp32-level accuracy; head_dim 64, 128-row tiles.  Warp-specialised: a
+   * split warp group prepares the K/V operand stages, QK^T and PV are issued
+   * by two warps (one issuing thread sustains only ~2/3 of the tensor core's
+   * rate at N = 64), and the O accumulator lives in tensor memory, rescaled
+   * only when a row's max grows by more than 2^8. */
   RAYA_KERNEL_TC32_WS = 34,
   /* The same pipeline in one resident CTA per SM that walks its 128-row
    * tiles back to back: each tile's q copy, key-tile splits and first QK^T
@@ -135,6 +132,25 @@ raya_attn_status raya_attn_forward_host(const raya_attn_desc* desc, const float*
                                         const float* v, size_t v_len, float* out,
                                         size_t out_len, const int32_t* valid_len,
                                         int device);
+
+/* The host-buffer call spread over several GPUs of this process: batch x
+ * heads is the shard.  The flattened batch*heads slices are cut into
+ * `ndevices` contiguous ranges balanced by allowed-pair count
+ * (raya_attn_shard); device devices[r] receives range r's q, k and v rows,
+ * runs the kernel on them and returns its part of the output, all devices at
+ * once (one host thread each; the reference's counterpart is Tiled's task
+ * split over (head, block) on host threads, tiled/mod.rs:82-124).  Slices are
+ * independent, so the result is bit-identical to raya_attn_forward_host on
+ * one device.  Outputs go to the HOST buffer `out` and, when `out_device0` is
+ * not NULL, also to that DEVICE buffer of batch*heads*seq*head_dim floats on
+ * devices[0]: the other devices' parts are copied into it device to device
+ * (peer copies over NVLink).  `out` may be NULL when `out_device0` is given
+ * (out_len is then ignored).  Device ids must be distinct.  Synchronous;
+ * allocates staging buffers on each device like raya_attn_forward_host. */
+raya_attn_status raya_attn_forward_multi_gpu(const raya_attn_desc* desc, const float* q, size_t q_len,
+                                             const float* k, size_t k_len, const float* v, size_t v_len,
+                                             float* out, size_t out_len, const int32_t* valid_len,
+                                             const int* devices, int ndevices, float* out_device0);
 
 /* Asynchronous device-buffer call on `stream` (the B200-native entry point,
  * no reference counterpart beyond the trait's semantics).  q, k, v, out are
@@ -227,6 +243,16 @@ raya_attn_status raya_attn_probe_timeout(int64_t timeout_cycles, void* stream);
 /* Message of the last error raised on the calling thread (KernelError's
  * Display text for the reference's errors).  Never NULL. */
 const char* raya_attn_last_error(void);
+
+/* The last error raised on the calling thread, as data: *kind is its status
+ * code, RAYA_ATTN_OK if none; for RAYA_ATTN_ERR_LENGTH, *name is
+ * the buffer ("q", "k", "v", "out" or "workspace") and *got / *expected its
+ * element count and the count the shape asks for, the fields of
+ * KernelError::Length { name, got, expected } (attention.rs:13-18); for other
+ * kinds *name is "" and both counts 0.  Any output pointer may be NULL; the
+ * name stays valid until the thread's next failing call.  Always returns
+ * RAYA_ATTN_OK. */
+raya_attn_status raya_attn_last_error_info(int* kind, const char** name, size_t* got, size_t* expected);
 
 /* The kernel that raya_attn_forward, raya_attn_forward_host and
  * raya_attn_forward_ex(RAYA_KERNEL_AUTO) launch for this descriptor, or with

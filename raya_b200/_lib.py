@@ -15,8 +15,6 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libraya_attn.so")
 OK, ERR_SHAPE, ERR_LENGTH, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_NCCL = range(7)
 MASK_BLOCK, MASK_WINDOW, MASK_FULL = 0, 1, 2
 KERNEL_AUTO, KERNEL_TILED64, KERNEL_ROWWISE = 0, 1, 2
-KERNEL_TC32 = 32
-KERNEL_TC32_PIPE = 33
 KERNEL_TC32_WS = 34
 KERNEL_TC32_STREAM = 36
 KERNEL_TC32_WS2 = 37
@@ -29,7 +27,8 @@ EXPORTS = (
     "raya_attn_work", "raya_attn_shard", "raya_attn_fill_normal",
     "raya_attn_ffma_peak", "raya_attn_version", "raya_attn_forward_timed",
     "raya_attn_probe_timeout", "raya_attn_forward_packed", "raya_attn_packed_workspace",
-    "raya_attn_forward_packed_noalloc", "raya_attn_kernel_for",
+    "raya_attn_forward_packed_noalloc", "raya_attn_kernel_for", "raya_attn_last_error_info",
+    "raya_attn_forward_multi_gpu",
 )
 
 
@@ -82,6 +81,12 @@ def _load() -> ctypes.CDLL:
     lib.raya_attn_sync_status.restype = st
     lib.raya_attn_last_error.argtypes = []
     lib.raya_attn_last_error.restype = ctypes.c_char_p
+    lib.raya_attn_last_error_info.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_char_p),
+                                              ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]
+    lib.raya_attn_last_error_info.restype = st
+    lib.raya_attn_forward_multi_gpu.argtypes = [dp, fp, sz, fp, sz, fp, sz, fp, sz, ip,
+                                                ctypes.POINTER(ctypes.c_int), ctypes.c_int, vp]
+    lib.raya_attn_forward_multi_gpu.restype = st
     lib.raya_attn_work.argtypes = [dp, ip, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]
     lib.raya_attn_work.restype = st
     lib.raya_attn_shard.argtypes = [dp, ip, ctypes.c_int, ctypes.c_int,

@@ -71,17 +71,34 @@ _ERRORS = {
 }
 
 
-def _check(status: int, lengths: dict | None = None) -> None:
+@dataclass(frozen=True)
+class ErrorInfo:
+    """The calling thread's last library error as data
+    (``raya_attn_last_error_info``): ``kind`` is the status code; ``name``,
+    ``got`` and ``expected`` are KernelError::Length's fields
+    (attention.rs:13-18) for length errors, else "", 0, 0."""
+
+    kind: int
+    name: str
+    got: int
+    expected: int
+
+
+def last_error_info() -> ErrorInfo:
+    kind, name = ctypes.c_int(), ctypes.c_char_p()
+    got, expected = ctypes.c_size_t(), ctypes.c_size_t()
+    lib.raya_attn_last_error_info(ctypes.byref(kind), ctypes.byref(name), ctypes.byref(got), ctypes.byref(expected))
+    return ErrorInfo(kind.value, (name.value or b"").decode(), got.value, expected.value)
+
+
+def _check(status: int) -> None:
     if status == _lib.OK:
         return
     msg = _lib.last_error()
     cls = _ERRORS.get(status, KernelError)
     if cls is LengthError:
-        # "buffer `q` has length 3, expected 32"
-        name = msg.split("`")[1] if "`" in msg else ""
-        got = lengths.get(name, 0) if lengths else 0
-        expected = int(msg.rsplit(" ", 1)[-1]) if msg[-1:].isdigit() else 0
-        raise LengthError(msg, name=name, got=got, expected=expected)
+        info = last_error_info()
+        raise LengthError(msg, name=info.name, got=info.got, expected=info.expected)
     raise cls(msg)
 
 
@@ -212,7 +229,7 @@ def validate(shape: AttnShape, params: AttnParams, q, k, v, out) -> None:
     lens = {n: int(np.asarray(b).size) for n, b in (("q", q), ("k", k), ("v", v), ("out", out))}
     d = make_desc(shape, params)
     _check(lib.raya_attn_validate(ctypes.byref(d), _i32p(valid), lens["q"], lens["k"], lens["v"],
-                                  lens["out"]), lens)
+                                  lens["out"]))
 
 
 def work(shape: AttnShape, params: AttnParams) -> tuple[int, int]:
@@ -222,6 +239,29 @@ def work(shape: AttnShape, params: AttnParams) -> tuple[int, int]:
     pairs, rows = ctypes.c_uint64(), ctypes.c_uint64()
     _check(lib.raya_attn_work(ctypes.byref(d), _i32p(valid), ctypes.byref(pairs), ctypes.byref(rows)))
     return pairs.value, rows.value
+
+
+def multi_gpu(shape: AttnShape, params: AttnParams, q, k, v, out=None, devices: Sequence[int] = (0,),
+              out_device0=None) -> None:
+    """The host-buffer call over several GPUs of this process
+    (``raya_attn_forward_multi_gpu``): batch x heads slices split by
+    allowed-pair count, one range per device, all devices at once.  ``out``
+    is a host float32 array or None; ``out_device0`` (a CUDA float32 tensor
+    of the whole output on ``devices[0]``, or None) also receives every
+    device's part by peer copies.  Synchronous."""
+    valid = params.valid_array(shape.batch)
+    qh, kh, vh = _host_f32("q", q), _host_f32("k", k), _host_f32("v", v)
+    oh = _host_f32("out", out, writable=True) if out is not None else None
+    devs = (ctypes.c_int * len(devices))(*devices)
+    d0 = None
+    if out_device0 is not None:
+        if not out_device0.is_cuda or not out_device0.is_contiguous() or out_device0.device.index != devices[0]:
+            raise TypeError("out_device0 must be a contiguous CUDA tensor on devices[0]")
+        d0 = out_device0.data_ptr()
+    d = make_desc(shape, params)
+    _check(lib.raya_attn_forward_multi_gpu(ctypes.byref(d), _f32p(qh), qh.size, _f32p(kh), kh.size, _f32p(vh),
+                                           vh.size, _f32p(oh) if oh is not None else None,
+                                           oh.size if oh is not None else 0, _i32p(valid), devs, len(devices), d0))
 
 
 def kernel_for(shape: AttnShape, params: AttnParams, packed: bool = False, rope: bool = False) -> int:
@@ -276,11 +316,10 @@ class Cuda(AttentionKernel):
         valid = params.valid_array(shape.batch)
         qh, kh, vh = _host_f32("q", q), _host_f32("k", k), _host_f32("v", v)
         oh = _host_f32("out", out, writable=True)
-        lens = {"q": qh.size, "k": kh.size, "v": vh.size, "out": oh.size}
         d = make_desc(shape, params)
         _check(lib.raya_attn_forward_host(ctypes.byref(d), _f32p(qh), qh.size, _f32p(kh), kh.size,
                                           _f32p(vh), vh.size, _f32p(oh), oh.size, _i32p(valid),
-                                          self.config.device), lens)
+                                          self.config.device))
 
     def attend_device(self, shape: AttnShape, params: AttnParams, q, k, v, out,
                       valid_len=None, stream=None, kernel: int | None = None) -> None:

@@ -14,13 +14,13 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/raya_attn.h"
 #include "common.cuh"
 #include "rowwise.cuh"
-#include "tc32.cuh"
-#include "tc32_pipe.cuh"
+#include "tc32_common.cuh"
 #include "tc32_ws.cuh"
 #include "tc32_stream.cuh"
 #include "tiled64.cuh"
@@ -139,6 +139,14 @@ int packed_kernel(const raya_attn_desc* d, bool rope) {
 __device__ int g_status;
 
 thread_local std::string t_error = "no error";
+// The last error as data (raya_attn_last_error_info): its status, and for
+// RAYA_ATTN_ERR_LENGTH the buffer name and the two element counts.
+struct ErrorInfo {
+  int kind = RAYA_ATTN_OK;
+  std::string name;
+  size_t got = 0, expected = 0;
+};
+thread_local ErrorInfo t_info;
 
 // cuTensorMapEncodeTiled, fetched once from the driver through the runtime
 // (no libcuda link dependency).
@@ -152,7 +160,19 @@ raya_attn_status fail(raya_attn_status st, const char* fmt, ...) {
   vsnprintf(buf, sizeof buf, fmt, ap);
   va_end(ap);
   t_error = buf;
+  t_info = ErrorInfo{};
+  t_info.kind = st;
   return st;
+}
+
+// KernelError::Length { name, got, expected } with its Display text
+// (attention.rs:13-18, 159-168).
+raya_attn_status fail_length(const char* name, size_t got, size_t expected) {
+  fail(RAYA_ATTN_ERR_LENGTH, "buffer `%s` has length %zu, expected %zu", name, got, expected);
+  t_info.name = name;
+  t_info.got = got;
+  t_info.expected = expected;
+  return RAYA_ATTN_ERR_LENGTH;
 }
 
 raya_attn_status cuda_fail(cudaError_t e, const char* what) {
@@ -194,12 +214,6 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tiled64 smem)");
       }
     }
-    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_fwd),
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::smem_bytes()));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32 smem)");
-    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_pipe_fwd),
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::pipe_smem_bytes()));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_pipe smem)");
     for (auto fn : {tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 1>, tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 2>,
                     tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 4>,
                     tc32::tc32_ws_fwd<tiled64::kPacked, false, 1>, tc32::tc32_ws_fwd<tiled64::kPacked, true, 1>,
@@ -422,23 +436,8 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     if (st != RAYA_ATTN_OK) return st;
     auto fn = stage_cycles ? tv->timed : tv->fn;
     fn<<<static_cast<unsigned>(grid), tv->warps * 32, tv->smem, stream>>>(a, maps);
-  } else if (kernel_id == RAYA_KERNEL_TC32 && !stage_cycles) {
-    if (d->head_dim != 64)
-      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tensor-core kernel needs head_dim 64, got %lld",
-                  static_cast<long long>(d->head_dim));
-    a.row_tiles = static_cast<int>((d->seq + tc32::kBM - 1) / tc32::kBM);
-    const long long grid = static_cast<long long>(d->batch) * d->heads * a.row_tiles;
-    if (grid > 0x7fffffffll)
-      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
-    tiled64::TmaMaps maps;
-    const uint64_t rows = static_cast<uint64_t>(d->batch) * d->heads * d->seq;
-    raya_attn_status st = encode_rows64(&maps.q, q, rows, tc32::kBM);
-    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.k, k, rows, tc32::kBN);
-    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tc32::kBN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
-    if (st != RAYA_ATTN_OK) return st;
-    tc32::tc32_fwd<<<static_cast<unsigned>(grid), tc32::kThreads, tc32::smem_bytes(), stream>>>(a, maps);
-  } else if ((kernel_id == RAYA_KERNEL_TC32_PIPE || kernel_id == RAYA_KERNEL_TC32_WS ||
-              kernel_id == RAYA_KERNEL_TC32_WS2 || kernel_id == RAYA_KERNEL_TC32_STREAM) &&
+  } else if ((kernel_id == RAYA_KERNEL_TC32_WS || kernel_id == RAYA_KERNEL_TC32_WS2 ||
+              kernel_id == RAYA_KERNEL_TC32_STREAM) &&
              !stage_cycles) {
     if (d->head_dim != 64)
       return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tensor-core kernel needs head_dim 64, got %lld",
@@ -468,12 +467,9 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     else if (kernel_id == RAYA_KERNEL_TC32_WS2 && a.row_tiles == 4)  // a whole slice of four row tiles per CTA
       tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 4>
           <<<static_cast<unsigned>((grid + 3) / 4), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
-    else if (kernel_id == RAYA_KERNEL_TC32_WS2)  // two 128-row tiles per CTA
+    else  // two 128-row tiles per CTA
       tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 2>
           <<<static_cast<unsigned>((grid + 1) / 2), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
-    else
-      tc32::tc32_pipe_fwd<<<static_cast<unsigned>(grid), tc32::kPipeThreads, tc32::pipe_smem_bytes(), stream>>>(
-          a, maps);
   } else if (stage_cycles) {
     return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: stage timing needs a tiled kernel");
   } else if (kernel_id == RAYA_KERNEL_ROWWISE) {
@@ -616,6 +612,181 @@ raya_attn_status rope_static_table(int dev, float2** out) {
   return RAYA_ATTN_OK;
 }
 
+// One valid length per (batch, head) slice, so that any range of slices is
+// an independent call (batch = #slices, heads = 1).
+std::vector<int32_t> slice_valid_lengths(const raya_attn_desc* d, const int32_t* valid_len) {
+  const int64_t nbh = d->batch * d->heads;
+  std::vector<int32_t> sv(static_cast<size_t>(nbh));
+  for (int64_t bh = 0; bh < nbh; ++bh)
+    sv[bh] = valid_len ? valid_len[bh / d->heads] : static_cast<int32_t>(d->seq);
+  return sv;
+}
+
+// The slices [bh0, bh1) of a validated call, run through one device:
+// host inputs q/k/v (whole tensors; the range is read at its offset), host
+// output `out` (or NULL), and optionally a DEVICE output `gather` of the
+// whole tensor on device `gather_dev` that receives this range (written by
+// the kernel itself when gather_dev is this device, else by peer copies).
+struct HostJob {
+  const raya_attn_desc* desc;
+  const int32_t* slice_valid;  // [batch*heads]
+  int64_t bh0, bh1;
+  const float *q, *k, *v;
+  float* out;
+  float* gather;
+  int gather_dev;
+};
+
+raya_attn_status host_pipeline(int device, const HostJob& job) {
+  const raya_attn_desc* desc = job.desc;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  DeviceCtx* ctx = nullptr;
+  raya_attn_status st = ensure_ready(device, &ctx);
+  if (st != RAYA_ATTN_OK) return st;
+  const bool direct = job.gather && job.gather_dev == device;  // the kernel writes into the gather buffer
+  const bool peer = job.gather && !direct;
+  if (peer) {
+    int can = 0;
+    e = cudaDeviceCanAccessPeer(&can, device, job.gather_dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceCanAccessPeer");
+    if (can) {
+      e = cudaDeviceEnablePeerAccess(job.gather_dev, 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();  // already on: not an error
+      } else if (e != cudaSuccess) {
+        return cuda_fail(e, "cudaDeviceEnablePeerAccess");
+      }
+    }
+  }
+  std::lock_guard<std::mutex> lock(ctx->mu);  // one host call per device at a time
+  if (!ctx->streams[0]) {
+    for (auto& sm : ctx->streams) {
+      e = cudaStreamCreateWithFlags(&sm, cudaStreamNonBlocking);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
+    }
+    e = cudaEventCreateWithFlags(&ctx->valid_ready, cudaEventDisableTiming);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+    for (int64_t c = 0; c < kMaxHostChunks; ++c) {
+      e = cudaEventCreateWithFlags(&ctx->chunk_in[c], cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->chunk_done[c], cudaEventDisableTiming);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+    }
+  }
+  const int64_t nbh = job.bh1 - job.bh0;
+  const size_t slice = static_cast<size_t>(desc->seq) * desc->head_dim;
+  const size_t n = static_cast<size_t>(nbh) * slice;
+  if (ctx->cap < n) {
+    for (auto& p : ctx->buf) {
+      if (p) cudaFree(p);
+      p = nullptr;
+    }
+    ctx->cap = 0;
+    for (auto& p : ctx->buf) {
+      e = cudaMalloc(&p, n * sizeof(float));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(staging)");
+    }
+    ctx->cap = n;
+  }
+  if (ctx->vcap < static_cast<size_t>(nbh)) {
+    if (ctx->dvalid) cudaFree(ctx->dvalid);
+    ctx->dvalid = nullptr;
+    ctx->vcap = 0;
+    e = cudaMalloc(&ctx->dvalid, nbh * sizeof(int32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(valid_len)");
+    ctx->vcap = nbh;
+  }
+  ctx->slice_valid.assign(job.slice_valid + job.bh0, job.slice_valid + job.bh1);
+  e = cudaMemcpyAsync(ctx->dvalid, ctx->slice_valid.data(), nbh * sizeof(int32_t), cudaMemcpyHostToDevice,
+                      ctx->streams[0]);
+  if (e != cudaSuccess) return cuda_fail(e, "copy valid_len to device");
+  e = cudaEventRecord(ctx->valid_ready, ctx->streams[0]);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+
+  // Pipeline over chunks of slices: stream 0 copies every chunk in, back to
+  // back; stream 1 runs chunk c's kernel once its inputs are in; stream 2
+  // copies chunk c out once its kernel is done.  The host-to-device copy
+  // engine (the bound: 3/4 of the bytes) never waits for a kernel or an
+  // outgoing copy, which one stream per chunk made it do.
+  const size_t bytes_total = 4 * n * sizeof(float);
+  const int64_t nchunks = std::max<int64_t>(
+      1, std::min<int64_t>({nbh, kMaxHostChunks,
+                            static_cast<int64_t>(std::llround(std::sqrt(static_cast<double>(bytes_total) / kHostChunkUnit)))}));
+  const float* src[3] = {job.q, job.k, job.v};
+  for (int64_t c = 0; c < nchunks; ++c) {
+    // Chunk c spans weight 2, the last two (with 3+ chunks) weight 1: a shorter tail.
+    auto cum = [&](int64_t i) {
+      const int64_t big = nchunks >= 3 ? nchunks - 2 : nchunks;
+      return 2 * std::min(i, big) + std::max<int64_t>(0, i - big);
+    };
+    const int64_t wt = cum(nchunks);
+    const int64_t c0 = nbh * cum(c) / wt, c1 = nbh * cum(c + 1) / wt;  // slices of this range
+    if (c1 <= c0) continue;
+    cudaStream_t s_in = ctx->streams[0], s_run = ctx->streams[1], s_out = ctx->streams[2];
+    const size_t off = static_cast<size_t>(c0) * slice;              // in the staging buffers
+    const size_t abs = static_cast<size_t>(job.bh0 + c0) * slice;    // in the caller's tensors
+    const size_t cnt = static_cast<size_t>(c1 - c0) * slice;
+    // Only the valid rows of each slice go in: no kernel reads q, k or v rows
+    // at or past valid_len (keys there are masked, V rows there are zeroed in
+    // shared memory, q rows there are read as zero), so whatever the staging
+    // buffers hold there does not reach the output.  One 2-D copy per run of
+    // slices with the same valid length (rows of `valid` * head_dim floats,
+    // pitch seq * head_dim).
+    for (int64_t r0 = c0; r0 < c1;) {
+      const int32_t vl = ctx->slice_valid[r0];
+      int64_t r1 = r0 + 1;
+      while (r1 < c1 && ctx->slice_valid[r1] == vl) ++r1;
+      if (vl > 0) {
+        const size_t pitch = slice * sizeof(float);
+        const size_t width = static_cast<size_t>(vl) * desc->head_dim * sizeof(float);
+        const size_t o = static_cast<size_t>(r0) * slice;
+        const size_t oa = static_cast<size_t>(job.bh0 + r0) * slice;
+        for (int i = 0; i < 3; ++i) {
+          e = cudaMemcpy2DAsync(ctx->buf[i] + o, pitch, src[i] + oa, pitch, width, static_cast<size_t>(r1 - r0),
+                                cudaMemcpyHostToDevice, s_in);
+          if (e != cudaSuccess) return cuda_fail(e, "copy inputs to device");
+        }
+      }
+      r0 = r1;
+    }
+    e = cudaEventRecord(ctx->chunk_in[c], s_in);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s_run, ctx->chunk_in[c], 0);
+    if (e == cudaSuccess && c == 0) e = cudaStreamWaitEvent(s_run, ctx->valid_ready, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "chunk events");
+    raya_attn_desc sub = *desc;
+    sub.batch = c1 - c0;
+    sub.heads = 1;
+    float* kout = direct ? job.gather + abs : ctx->buf[3] + off;
+    st = launch_on(ctx, &sub, ctx->buf[0] + off, ctx->buf[1] + off, ctx->buf[2] + off, kout, ctx->dvalid + c0,
+                   s_run, RAYA_KERNEL_AUTO);
+    if (st != RAYA_ATTN_OK) return st;
+    e = cudaEventRecord(ctx->chunk_done[c], s_run);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s_out, ctx->chunk_done[c], 0);
+    if (e != cudaSuccess) return cuda_fail(e, "chunk events");
+    if (job.out) {
+      e = cudaMemcpyAsync(job.out + abs, kout, cnt * sizeof(float), cudaMemcpyDeviceToHost, s_out);
+      if (e != cudaSuccess) return cuda_fail(e, "copy out to host");
+    }
+    if (peer) {
+      e = cudaMemcpyPeerAsync(job.gather + abs, job.gather_dev, kout, device, cnt * sizeof(float), s_out);
+      if (e != cudaSuccess) return cuda_fail(e, "peer copy to the gather buffer");
+    }
+  }
+  for (auto& sm : ctx->streams) {
+    e = cudaStreamSynchronize(sm);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  }
+  int flag = 0;
+  e = cudaMemcpy(&flag, ctx->status, sizeof flag, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read status");
+  if (flag != 0) {
+    const int zero = 0;
+    cudaMemcpy(ctx->status, &zero, sizeof zero, cudaMemcpyHostToDevice);
+    return fail(RAYA_ATTN_ERR_TIMEOUT, "timeout: a device-side wait gave up (status 0x%x)", flag);
+  }
+  return RAYA_ATTN_OK;
+}
+
 }  // namespace
 }  // namespace raya
 
@@ -627,6 +798,14 @@ int raya_attn_version(void) { return RAYA_ATTN_VERSION; }
 
 const char* raya_attn_last_error(void) { return t_error.c_str(); }
 
+raya_attn_status raya_attn_last_error_info(int* kind, const char** name, size_t* got, size_t* expected) {
+  if (kind) *kind = t_info.kind;
+  if (name) *name = t_info.name.c_str();
+  if (got) *got = t_info.got;
+  if (expected) *expected = t_info.expected;
+  return RAYA_ATTN_OK;
+}
+
 raya_attn_status raya_attn_validate(const raya_attn_desc* desc, const int32_t* valid_len,
                                     size_t q_len, size_t k_len, size_t v_len, size_t out_len) {
   raya_attn_status st = check_shape(desc);
@@ -637,9 +816,7 @@ raya_attn_status raya_attn_validate(const raya_attn_desc* desc, const int32_t* v
   const struct { const char* name; size_t got; } bufs[4] = {
       {"q", q_len}, {"k", k_len}, {"v", v_len}, {"out", out_len}};
   for (const auto& b : bufs)  // attention.rs:159-168
-    if (b.got != expected)
-      return fail(RAYA_ATTN_ERR_LENGTH, "buffer `%s` has length %zu, expected %zu", b.name, b.got,
-                  expected);
+    if (b.got != expected) return fail_length(b.name, b.got, expected);
   return RAYA_ATTN_OK;
 }
 
@@ -749,7 +926,7 @@ raya_attn_status raya_attn_forward_packed(const raya_attn_desc* desc, const floa
   size_t need = 0;
   raya_attn_packed_workspace(desc, rope_theta, &need);
   if (rope && (!workspace || workspace_bytes < need))
-    return fail(RAYA_ATTN_ERR_LENGTH, "buffer `workspace` has length %zu, expected %zu", workspace_bytes, need);
+    return fail_length("workspace", workspace_bytes, need);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -857,133 +1034,79 @@ raya_attn_status raya_attn_forward_host(const raya_attn_desc* desc, const float*
                                         int device) {
   raya_attn_status st = raya_attn_validate(desc, valid_len, q_len, k_len, v_len, out_len);
   if (st != RAYA_ATTN_OK) return st;
-  const size_t n = numel(desc);
-  if (n == 0) return RAYA_ATTN_OK;
+  if (numel(desc) == 0) return RAYA_ATTN_OK;
   if (!q || !k || !v || !out) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null buffer");
-  cudaError_t e = cudaSetDevice(device);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
-  DeviceCtx* ctx = nullptr;
-  st = ensure_ready(device, &ctx);
-  if (st != RAYA_ATTN_OK) return st;
-  std::lock_guard<std::mutex> lock(ctx->mu);  // one host call per device at a time
-  if (!ctx->streams[0]) {
-    for (auto& sm : ctx->streams) {
-      e = cudaStreamCreateWithFlags(&sm, cudaStreamNonBlocking);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate");
-    }
-    e = cudaEventCreateWithFlags(&ctx->valid_ready, cudaEventDisableTiming);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
-    for (int64_t c = 0; c < kMaxHostChunks; ++c) {
-      e = cudaEventCreateWithFlags(&ctx->chunk_in[c], cudaEventDisableTiming);
-      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->chunk_done[c], cudaEventDisableTiming);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
-    }
-  }
-  if (ctx->cap < n) {
-    for (auto& p : ctx->buf) {
-      if (p) cudaFree(p);
-      p = nullptr;
-    }
-    ctx->cap = 0;
-    for (auto& p : ctx->buf) {
-      e = cudaMalloc(&p, n * sizeof(float));
-      if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(staging)");
-    }
-    ctx->cap = n;
-  }
-  // One valid length per (batch, head) slice, so that any range of slices is
-  // an independent call (batch = #slices, heads = 1).
-  const int64_t nbh = desc->batch * desc->heads;
-  if (ctx->vcap < static_cast<size_t>(nbh)) {
-    if (ctx->dvalid) cudaFree(ctx->dvalid);
-    ctx->dvalid = nullptr;
-    ctx->vcap = 0;
-    e = cudaMalloc(&ctx->dvalid, nbh * sizeof(int32_t));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(valid_len)");
-    ctx->vcap = nbh;
-  }
-  ctx->slice_valid.resize(nbh);
-  for (int64_t bh = 0; bh < nbh; ++bh)
-    ctx->slice_valid[bh] = valid_len ? valid_len[bh / desc->heads] : static_cast<int32_t>(desc->seq);
-  e = cudaMemcpyAsync(ctx->dvalid, ctx->slice_valid.data(), nbh * sizeof(int32_t), cudaMemcpyHostToDevice,
-                      ctx->streams[0]);
-  if (e != cudaSuccess) return cuda_fail(e, "copy valid_len to device");
-  e = cudaEventRecord(ctx->valid_ready, ctx->streams[0]);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  const std::vector<int32_t> sv = slice_valid_lengths(desc, valid_len);
+  HostJob job{desc, sv.data(), 0, desc->batch * desc->heads, q, k, v, out, nullptr, -1};
+  return host_pipeline(device, job);
+}
 
-  // Pipeline over chunks of slices: stream 0 copies every chunk in, back to
-  // back; stream 1 runs chunk c's kernel once its inputs are in; stream 2
-  // copies chunk c out once its kernel is done.  The host-to-device copy
-  // engine (the bound: 3/4 of the bytes) never waits for a kernel or an
-  // outgoing copy, which one stream per chunk made it do.
-  const size_t slice = static_cast<size_t>(desc->seq) * desc->head_dim;
-  const size_t bytes_total = 4 * n * sizeof(float);
-  const int64_t nchunks = std::max<int64_t>(
-      1, std::min<int64_t>({nbh, kMaxHostChunks,
-                            static_cast<int64_t>(std::llround(std::sqrt(static_cast<double>(bytes_total) / kHostChunkUnit)))}));
-  const float* src[3] = {q, k, v};
-  for (int64_t c = 0; c < nchunks; ++c) {
-    // Chunk c spans weight 2, the last two (with 3+ chunks) weight 1: a shorter tail.
-    auto cum = [&](int64_t i) {
-      const int64_t big = nchunks >= 3 ? nchunks - 2 : nchunks;
-      return 2 * std::min(i, big) + std::max<int64_t>(0, i - big);
-    };
-    const int64_t wt = cum(nchunks);
-    const int64_t bh0 = nbh * cum(c) / wt, bh1 = nbh * cum(c + 1) / wt;
-    if (bh1 <= bh0) continue;
-    cudaStream_t s_in = ctx->streams[0], s_run = ctx->streams[1], s_out = ctx->streams[2];
-    const size_t off = static_cast<size_t>(bh0) * slice;
-    const size_t cnt = static_cast<size_t>(bh1 - bh0) * slice;
-    // Only the valid rows of each slice go in: no kernel reads q, k or v rows
-    // at or past valid_len (keys there are masked, V rows there are zeroed in
-    // shared memory, q rows there are read as zero), so whatever the staging
-    // buffers hold there does not reach the output.  One 2-D copy per run of
-    // slices with the same valid length (rows of `valid` * head_dim floats,
-    // pitch seq * head_dim).
-    for (int64_t r0 = bh0; r0 < bh1;) {
-      const int32_t vl = ctx->slice_valid[r0];
-      int64_t r1 = r0 + 1;
-      while (r1 < bh1 && ctx->slice_valid[r1] == vl) ++r1;
-      if (vl > 0) {
-        const size_t pitch = slice * sizeof(float);
-        const size_t width = static_cast<size_t>(vl) * desc->head_dim * sizeof(float);
-        const size_t o = static_cast<size_t>(r0) * slice;
-        for (int i = 0; i < 3; ++i) {
-          e = cudaMemcpy2DAsync(ctx->buf[i] + o, pitch, src[i] + o, pitch, width, static_cast<size_t>(r1 - r0),
-                                cudaMemcpyHostToDevice, s_in);
-          if (e != cudaSuccess) return cuda_fail(e, "copy inputs to device");
-        }
-      }
-      r0 = r1;
-    }
-    e = cudaEventRecord(ctx->chunk_in[c], s_in);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(s_run, ctx->chunk_in[c], 0);
-    if (e == cudaSuccess && c == 0) e = cudaStreamWaitEvent(s_run, ctx->valid_ready, 0);
-    if (e != cudaSuccess) return cuda_fail(e, "chunk events");
-    raya_attn_desc sub = *desc;
-    sub.batch = bh1 - bh0;
-    sub.heads = 1;
-    st = launch_on(ctx, &sub, ctx->buf[0] + off, ctx->buf[1] + off, ctx->buf[2] + off, ctx->buf[3] + off,
-                   ctx->dvalid + bh0, s_run, RAYA_KERNEL_AUTO);
+raya_attn_status raya_attn_forward_multi_gpu(const raya_attn_desc* desc, const float* q, size_t q_len,
+                                             const float* k, size_t k_len, const float* v, size_t v_len,
+                                             float* out, size_t out_len, const int32_t* valid_len,
+                                             const int* devices, int ndevices, float* out_device0) {
+  raya_attn_status st = check_shape(desc);
+  if (st != RAYA_ATTN_OK) return st;
+  if (!out && !out_device0) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: no output buffer");
+  st = raya_attn_validate(desc, valid_len, q_len, k_len, v_len, out ? out_len : numel(desc));
+  if (st != RAYA_ATTN_OK) return st;
+  if (!devices || ndevices < 1 || ndevices > kMaxDevices)
+    return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: %d devices (1 to %d)", ndevices, kMaxDevices);
+  for (int i = 0; i < ndevices; ++i) {
+    if (devices[i] < 0 || devices[i] >= kMaxDevices)
+      return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: device id %d", devices[i]);
+    for (int j = 0; j < i; ++j)
+      if (devices[j] == devices[i])
+        return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: device %d listed twice", devices[i]);
+  }
+  if (numel(desc) == 0) return RAYA_ATTN_OK;
+  if (!q || !k || !v) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null buffer");
+  if (out_device0 && !aligned16(out_device0))
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: tensors must be 16-byte aligned");
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+  for (int i = 0; i < ndevices; ++i)
+    if (devices[i] >= count)
+      return fail(RAYA_ATTN_ERR_CUDA, "cuda: device %d of %d", devices[i], count);
+  const std::vector<int32_t> sv = slice_valid_lengths(desc, valid_len);
+  // The partition of raya_attn_shard, one range per device.
+  std::vector<int64_t> lo(ndevices), hi(ndevices);
+  for (int r = 0; r < ndevices; ++r) {
+    int64_t b = 0, en = 0;
+    st = raya_attn_shard(desc, valid_len, ndevices, r, &b, &en);
     if (st != RAYA_ATTN_OK) return st;
-    e = cudaEventRecord(ctx->chunk_done[c], s_run);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(s_out, ctx->chunk_done[c], 0);
-    if (e != cudaSuccess) return cuda_fail(e, "chunk events");
-    e = cudaMemcpyAsync(out + off, ctx->buf[3] + off, cnt * sizeof(float), cudaMemcpyDeviceToHost, s_out);
-    if (e != cudaSuccess) return cuda_fail(e, "copy out to host");
+    lo[r] = b;
+    hi[r] = en;
   }
-  for (auto& sm : ctx->streams) {
-    e = cudaStreamSynchronize(sm);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  // One host thread per device; each runs the host-buffer pipeline on its
+  // range.  Errors are raised on the worker's thread and handed back here.
+  struct Result {
+    raya_attn_status st = RAYA_ATTN_OK;
+    std::string msg;
+    ErrorInfo info;
+  };
+  std::vector<Result> res(ndevices);
+  std::vector<std::thread> pool;
+  pool.reserve(ndevices);
+  for (int r = 0; r < ndevices; ++r) {
+    pool.emplace_back([&, r] {
+      if (hi[r] <= lo[r]) return;
+      HostJob job{desc, sv.data(), lo[r], hi[r], q, k, v, out, out_device0, devices[0]};
+      res[r].st = host_pipeline(devices[r], job);
+      if (res[r].st != RAYA_ATTN_OK) {
+        res[r].msg = t_error;
+        res[r].info = t_info;
+      }
+    });
   }
-  int flag = 0;
-  e = cudaMemcpy(&flag, ctx->status, sizeof flag, cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_fail(e, "read status");
-  if (flag != 0) {
-    const int zero = 0;
-    cudaMemcpy(ctx->status, &zero, sizeof zero, cudaMemcpyHostToDevice);
-    return fail(RAYA_ATTN_ERR_TIMEOUT, "timeout: a device-side wait gave up (status 0x%x)", flag);
-  }
+  for (auto& t : pool) t.join();
+  for (int r = 0; r < ndevices; ++r)
+    if (res[r].st != RAYA_ATTN_OK) {
+      t_error = res[r].msg;
+      t_info = res[r].info;
+      return res[r].st;
+    }
   return RAYA_ATTN_OK;
 }
 

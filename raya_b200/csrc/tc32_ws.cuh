@@ -1,9 +1,10 @@
 // tc32_ws.cuh — 3xTF32 tensor-core attention with two MMA-issuing warps and
 // the O accumulator in tensor memory (sm_100a).
 //
-// The arithmetic of tc32_pipe_fwd (raw fp32 tiles as the hi operands, lo =
-// x - trunc(x), three tcgen05.mma products per tile), with the two changes
-// that its measurements asked for:
+// 3xTF32 (tc32_common.cuh: raw fp32 tiles as the hi operands, lo =
+// x - trunc(x), three tcgen05.mma products per tile), warp-specialised so
+// that the tensor core, the softmax and the operand split overlap, with two
+// measured refinements over a single-issuer pipeline:
 //
 //   * Two issuing threads.  One thread issuing tcgen05.mma kind::tf32 at
 //     M = 128, N = 64 sustains one instruction per ~47.5 cycles; two threads
@@ -49,7 +50,7 @@
 // (bounded) before tensor memory is freed.
 #pragma once
 
-#include "tc32_pipe.cuh"
+#include "tc32_common.cuh"
 
 namespace raya {
 namespace tc32 {

@@ -8,8 +8,9 @@ head) slice reads only its own q, k, v.  So the multi-GPU path is:
   2. rank r generates or receives only its slices and runs the kernel on
      them as an independent call (``shard_problem``: the range re-expressed as
      ``batch = #slices, heads = 1`` with one valid length per slice);
-  3. optionally the output shards are gathered to rank 0 with one
-     ``torch.distributed.gather`` (NCCL over NVLink on GPUs, gloo on CPU).
+  3. optionally the output shards are gathered to rank 0
+     (``gather_to_rank0``: point-to-point receives straight into rank 0's
+     output tensor, NCCL over NVLink on GPUs, gloo on CPU).
 
 There is no collective on the compute path.
 """
@@ -55,21 +56,34 @@ def shard_problem(shape: AttnShape, params: AttnParams, begin: int, end: int):
     return sub_shape, sub_params
 
 
-def gather_to_rank0(local, sp: ShardPlan, rank: int, group=None):
+def gather_to_rank0(local, sp: ShardPlan, rank: int, group=None, out=None):
     """Gathers every rank's output shard (a 1-D tensor of sp.elems(rank)
     floats) into one tensor on rank 0, in slice order; None on other ranks.
-    Shards are padded to the largest so a single gather moves them."""
+
+    Rank 0's result is ``out`` (the whole output, 1-D; allocated here when
+    None).  Each other rank's shard is received straight into its slice
+    range of ``out`` by point-to-point transfers (NCCL over NVLink between
+    GPUs, gloo on CPU), all posted at once; rank 0's own shard is copied in
+    only when ``local`` is not already that range of ``out`` (a kernel can
+    write it there directly).  Nothing is padded or concatenated."""
     import torch
     import torch.distributed as dist
 
-    n = sp.max_elems
-    buf = local
-    if local.numel() != n:
-        buf = torch.zeros(n, dtype=local.dtype, device=local.device)
-        buf[: local.numel()] = local
+    n = sp.slice_elems
     if rank == 0:
-        parts = [torch.empty(n, dtype=local.dtype, device=local.device) for _ in range(sp.world)]
-        dist.gather(buf, gather_list=parts, dst=0, group=group)
-        return torch.cat([parts[r][: sp.elems(r)] for r in range(sp.world)])
-    dist.gather(buf, dst=0, group=group)
+        total = sp.ranges[-1][1] * n
+        if out is None:
+            out = torch.empty(total, dtype=local.dtype, device=local.device)
+        b, e = sp.range(0)
+        own = out[b * n:e * n]
+        if e > b and own.data_ptr() != local.data_ptr():
+            own.copy_(local)
+        ops = [dist.P2POp(dist.irecv, out[rb * n:re * n], r, group)
+               for r, (rb, re) in enumerate(sp.ranges) if r > 0 and re > rb]
+        for req in (dist.batch_isend_irecv(ops) if ops else []):
+            req.wait()
+        return out
+    if sp.elems(rank) > 0:
+        for req in dist.batch_isend_irecv([dist.P2POp(dist.isend, local, 0, group)]):
+            req.wait()
     return None

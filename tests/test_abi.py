@@ -6,6 +6,7 @@ import ctypes
 import os
 import re
 import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -217,3 +218,61 @@ def test_automatic_kernel_choice(mask, block, expect_tc):
             assert rb.kernel_for(shape, params, packed=True, rope=rope) == rb._lib.KERNEL_TC32_WS
         else:
             assert rb.kernel_for(shape, params, packed=True, rope=rope) in _lib.KERNEL_TILED64_VARIANTS.values()
+
+
+def test_length_errors_carry_their_fields_as_data():
+    """KernelError::Length { name, got, expected } (attention.rs:13-18) comes
+    back from raya_attn_last_error_info, not from parsing the message."""
+    shape = _shape()
+    ok = np.zeros(shape.numel(), dtype=np.float32)
+    p = rb.AttnParams.new(rb.Mask.BLOCK3, 4, 8)
+    with pytest.raises(rb.LengthError):
+        rb.validate(shape, p, ok, ok, np.zeros(5, np.float32), ok)
+    info = rb.last_error_info()
+    assert (info.kind, info.name, info.got, info.expected) == (_lib.ERR_LENGTH, "v", 5, 32)
+    with pytest.raises(rb.ShapeError):
+        rb.validate(_shape(d=12), p, ok, ok, ok, ok)
+    info = rb.last_error_info()
+    assert (info.kind, info.name, info.got, info.expected) == (_lib.ERR_SHAPE, "", 0, 0)
+    # NULL outputs are allowed
+    assert _lib.lib.raya_attn_last_error_info(None, None, None, None) == _lib.OK
+
+
+def test_multi_gpu_call_validates_before_touching_a_gpu():
+    """raya_attn_forward_multi_gpu rejects bad arguments with the reference's
+    error kinds before any device work."""
+    shape = _shape(batch=2)
+    ok = np.zeros(shape.numel(), dtype=np.float32)
+    p = rb.AttnParams.new(rb.Mask.BLOCK3, 4, 8)
+    with pytest.raises(rb.LengthError) as e:
+        rb.multi_gpu(shape, p, ok[:7], ok, ok, ok.copy(), devices=[0, 1])
+    assert (e.value.name, e.value.got, e.value.expected) == ("q", 7, 64)
+    with pytest.raises(rb.ShapeError, match="listed twice"):
+        rb.multi_gpu(shape, p, ok, ok, ok, ok.copy(), devices=[1, 1])
+    with pytest.raises(rb.ShapeError, match="devices"):
+        rb.multi_gpu(shape, p, ok, ok, ok, ok.copy(), devices=[])
+    with pytest.raises(rb.ShapeError, match="no output"):
+        rb.multi_gpu(shape, p, ok, ok, ok, None, devices=[0])
+    with pytest.raises(rb.ShapeError, match="exceeds seq"):
+        rb.multi_gpu(shape, rb.AttnParams.new(rb.Mask.BLOCK3, [4, 5], 8), ok, ok, ok, ok.copy(), devices=[0])
+
+
+def test_no_cpu_fallback_when_the_library_is_missing(tmp_path):
+    """The package imports without loading the library (its workloads module
+    is plain numpy), but the first name that needs the CUDA library raises
+    ImportError when it is missing: there is no CPU path."""
+    code = (
+        "import sys; sys.path.insert(0, %r)\n"
+        "import raya_b200, raya_b200.workloads\n"
+        "maps = open('/proc/self/maps').read()\n"
+        "assert 'libraya_attn' not in maps, 'library mapped by a plain import'\n"
+        "from raya_b200 import _lib\n"
+        "_lib.LIB_PATH = %r\n"
+        "try:\n"
+        "    _lib._load()\n"
+        "except ImportError as e:\n"
+        "    print('raised:', e)\n"
+    ) % (ROOT, str(tmp_path / "missing.so"))
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr
+    assert "raised:" in out.stdout and "no fallback" in out.stdout

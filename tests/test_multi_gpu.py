@@ -84,3 +84,38 @@ def test_two_gpu_shards_gather_to_the_single_gpu_result(tmp_path):
     out = np.empty(shape.numel(), dtype=np.float32)
     rb.Cuda().attend(shape, params, q, k, v, out)
     assert np.array_equal(got, out)
+
+
+def _multi_problem():
+    import raya_b200 as rb
+
+    shape = rb.AttnShape(heads=5, seq=900, head_dim=64, batch=7)
+    params = rb.AttnParams.new(rb.Mask.block(1), [900, 1, 0, 513, 899, 640, 128], 64, block=128)
+    return shape, params
+
+
+@pytest.mark.parametrize("devices", [[0], [0, 1], [1, 0]], ids=["one", "two", "two-gather-on-1"])
+def test_multi_gpu_entry_point_equals_the_single_gpu_call(cuda_device, devices):
+    """raya_attn_forward_multi_gpu through the C ABI: slices split over the
+    devices by raya_attn_shard, host output and the device-side gather on
+    devices[0] both bit-identical to raya_attn_forward_host on one GPU."""
+    import torch
+
+    import oracle
+    import raya_b200 as rb
+
+    if max(devices) >= torch.cuda.device_count():
+        pytest.skip(f"needs {max(devices) + 1} GPUs")
+    shape, params = _multi_problem()
+    q, k, v = oracle.qkv(shape.numel(), 31)
+    want = np.empty(shape.numel(), dtype=np.float32)
+    rb.Cuda().attend(shape, params, q, k, v, want)
+    got = np.full(shape.numel(), 7.0, dtype=np.float32)
+    gathered = torch.full((shape.numel(),), -3.0, dtype=torch.float32, device=torch.device("cuda", devices[0]))
+    rb.multi_gpu(shape, params, q, k, v, got, devices=devices, out_device0=gathered)
+    assert np.array_equal(got, want)
+    assert np.array_equal(gathered.cpu().numpy(), want)
+    # the device-side gather alone (no host output)
+    gathered.fill_(5.0)
+    rb.multi_gpu(shape, params, q, k, v, None, devices=devices, out_device0=gathered)
+    assert np.array_equal(gathered.cpu().numpy(), want)
