@@ -475,7 +475,8 @@ def run_b200(args) -> None:
     # Stage proportions of one extra, instrumented launch (the reference
     # bench's "stages" field, benches/local_attention.rs:127-130,155-157).
     stages = None
-    if not args.packed and shape.batch > 0 and chosen in tiled_ids:
+    if not args.packed and shape.batch > 0 and (chosen in tiled_ids or chosen in (rb.KERNEL_TC32_WS,
+                                                                                  rb.KERNEL_TC32_WS2)):
         st = rb.stage_times(shape, params, q, k, v, out, valid_len=dvalid, kernel=chosen)
         stages = {key: round(val, 2) for key, val in st.items() if key.endswith("pct")}
 

@@ -110,7 +110,13 @@ typedef enum {
    * the whole slice; head-major layout), one after the other, each run as a
    * CTA of its own (sharing only the CTA's launch, tensor-memory allocation
    * and valid_len loads). */
-  RAYA_KERNEL_TC32_WS2 = 37
+  RAYA_KERNEL_TC32_WS2 = 37,
+  /* Two consecutive 128-row tiles of a slice per CTA sharing one K/V stream
+   * (each K/V tile loaded and split once for both), two softmax warp groups
+   * side by side, q tiles as shared-memory operands, and each key tile's PV
+   * product added into the O rows in fp32 registers (the tensor core's
+   * accumulation in tensor memory is biased toward zero over long chains). */
+  RAYA_KERNEL_TC32_PAIR = 38
 } raya_kernel_id;
 
 /* Argument checks of validate (attention.rs:128-170), extended to the batch
@@ -213,14 +219,23 @@ raya_attn_status raya_attn_forward_packed_noalloc(const raya_attn_desc* desc, co
                                                   const int32_t* valid_len, float rope_theta, void* stream);
 
 /* Stage timing, the counterpart of Tiled::attend_with_stages / StageTimes
- * (tiled/mod.rs:60-126, tiled/stages.rs:1-31): raya_attn_forward_ex with a
- * tiled kernel (kernel_id AUTO, TILED64 or a TILED64_* variant) whose warps
- * read clock64 around each stage and add their cycle counts into
- * stage_cycles, a DEVICE array of 8 uint64 that the caller zeroes:
- * [0] QK^T, [1] softmax, [2] P.V, [3] K-tile wait, [4] V-tile wait,
- * [5] next-tile refill, [6] warp-tiles processed, [7] total cycles.  Like the
- * reference's stage-timing build, the clocks perturb the run slightly: read
- * the counters as proportions. */
+ * (tiled/mod.rs:60-126, tiled/stages.rs:1-31): raya_attn_forward_ex whose
+ * kernel reads clock64 around each stage and adds the cycle counts into
+ * stage_cycles, a DEVICE array of 8 uint64 that the caller zeroes.
+ * kernel_id: RAYA_KERNEL_AUTO (the automatic choice; RAYA_KERNEL_TC32_WS
+ * where that is RAYA_KERNEL_TC32_STREAM), TILED64 or a TILED64_* variant, or
+ * RAYA_KERNEL_TC32_WS / RAYA_KERNEL_TC32_WS2.
+ * Tiled kernels (warp cycles summed over warps): [0] QK^T, [1] softmax,
+ * [2] P.V, [3] K-tile wait, [4] V-tile wait, [5] next-tile refill,
+ * [6] warp-tiles processed, [7] total cycles.
+ * Tensor-core kernels (cycles per CTA, summed over CTAs): [0] QK^T products
+ * in flight (issue to completion), [1] one softmax warp's work per key tile,
+ * [2] P.V products in flight, [3] the QK^T issuer waiting for K's operands,
+ * [4] the P.V issuer waiting for P and V's operands, [5] one split warp's
+ * operand preparation, [6] key tiles, [7] cycles from a 128-row tile's start
+ * to its output store.  These stages overlap in time.
+ * Like the reference's stage-timing build, the clocks perturb the run
+ * slightly: read the counters as proportions. */
 raya_attn_status raya_attn_forward_timed(const raya_attn_desc* desc, const float* q,
                                          const float* k, const float* v, float* out,
                                          const int32_t* valid_len, void* stream,

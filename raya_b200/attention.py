@@ -393,10 +393,13 @@ STAGE_NAMES = ("qk", "softmax", "pv", "k_wait", "v_wait", "refill", "tiles", "to
 
 def stage_times(shape: AttnShape, params: AttnParams, q, k, v, out, valid_len=None,
                 kernel: int = _lib.KERNEL_TILED64, stream=None) -> dict:
-    """Runs the tiled kernel once with per-stage clocks (the counterpart of
-    Tiled::attend_with_stages, tiled/mod.rs:60-126) and returns the summed
-    warp cycles per stage plus qk/softmax/pv percentages of their total
-    (StageTimes::percentages, tiled/stages.rs:19-31)."""
+    """Runs a kernel once with per-stage clocks (the counterpart of
+    Tiled::attend_with_stages, tiled/mod.rs:60-126) and returns the cycles
+    per stage plus qk/softmax/pv percentages of their total
+    (StageTimes::percentages, tiled/stages.rs:19-31).  ``kernel``: a tiled
+    kernel (warp cycles per stage), or KERNEL_TC32_WS / KERNEL_TC32_WS2 /
+    KERNEL_AUTO for the tensor-core kernels (per-CTA cycles of QK^T and PV
+    products in flight and of one softmax warp; these overlap in time)."""
     import torch
 
     dev = q.device

@@ -21,6 +21,7 @@
 #include "common.cuh"
 #include "rowwise.cuh"
 #include "tc32_common.cuh"
+#include "tc32_pair.cuh"
 #include "tc32_ws.cuh"
 #include "tc32_stream.cuh"
 #include "tiled64.cuh"
@@ -217,10 +218,17 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
     for (auto fn : {tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 1>, tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 2>,
                     tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 4>,
                     tc32::tc32_ws_fwd<tiled64::kPacked, false, 1>, tc32::tc32_ws_fwd<tiled64::kPacked, true, 1>,
-                    tc32::tc32_ws_fwd<tiled64::kPacked, false, 2>}) {
+                    tc32::tc32_ws_fwd<tiled64::kPacked, false, 2>, tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 1, true>,
+                    tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 2, true>,
+                    tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 4, true>}) {
       e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(tc32::pipe_smem_bytes()));
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_ws smem)");
+    }
+    for (auto fn : {tc32::tc32_pair_fwd<false>, tc32::tc32_pair_fwd<true>}) {
+      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(tc32::pair_smem_bytes()));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_pair smem)");
     }
     e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_stream_fwd),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::stream_smem_bytes()));
@@ -414,7 +422,12 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
   AttnArgs a = make_args(d, q, k, v, out, valid_len, ctx->status);
   a.stage_cycles = stage_cycles;
 
-  if (kernel_id == RAYA_KERNEL_AUTO) kernel_id = stage_cycles ? RAYA_KERNEL_TILED64 : auto_kernel(d);
+  if (kernel_id == RAYA_KERNEL_AUTO) {
+    kernel_id = auto_kernel(d);
+    // stage timing of the automatic choice, or of the two-issuer kernel where
+    // that is the persistent one (which has no timed build)
+    if (stage_cycles && kernel_id == RAYA_KERNEL_TC32_STREAM) kernel_id = RAYA_KERNEL_TC32_WS;
+  }
   if (kernel_id == RAYA_KERNEL_TILED64) kernel_id = tuned_tiled(d);
   const TiledVariant* tv = nullptr;
   for (const TiledVariant& t : kTiled)
@@ -436,9 +449,29 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     if (st != RAYA_ATTN_OK) return st;
     auto fn = stage_cycles ? tv->timed : tv->fn;
     fn<<<static_cast<unsigned>(grid), tv->warps * 32, tv->smem, stream>>>(a, maps);
-  } else if ((kernel_id == RAYA_KERNEL_TC32_WS || kernel_id == RAYA_KERNEL_TC32_WS2 ||
-              kernel_id == RAYA_KERNEL_TC32_STREAM) &&
-             !stage_cycles) {
+  } else if (kernel_id == RAYA_KERNEL_TC32_PAIR) {
+    if (d->head_dim != 64)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tensor-core kernel needs head_dim 64, got %lld",
+                  static_cast<long long>(d->head_dim));
+    a.row_tiles = static_cast<int>((d->seq + 2 * tc32::kBM - 1) / (2 * tc32::kBM));  // 256-row pairs per slice
+    const long long grid = static_cast<long long>(d->batch) * d->heads * a.row_tiles;
+    if (grid > 0x7fffffffll)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
+    const uint64_t rows = static_cast<uint64_t>(d->batch) * d->heads * d->seq;
+    if (rows > 0x7fffffffull)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %llu rows exceed the tensor-map row limit",
+                  static_cast<unsigned long long>(rows));
+    tc32::PipeMaps maps;
+    raya_attn_status st = encode_rows64(&maps.k, k, rows, tc32::kBN);
+    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tc32::kBN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    if (st == RAYA_ATTN_OK)
+      st = encode_slices3d(&maps.o, out, static_cast<uint64_t>(d->batch) * d->heads, static_cast<uint64_t>(d->seq));
+    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.q, q, rows, tc32::kBN);
+    if (st != RAYA_ATTN_OK) return st;
+    (stage_cycles ? tc32::tc32_pair_fwd<true> : tc32::tc32_pair_fwd<false>)
+        <<<static_cast<unsigned>(grid), tc32::kPairThreads, tc32::pair_smem_bytes(), stream>>>(a, maps);
+  } else if (kernel_id == RAYA_KERNEL_TC32_WS || kernel_id == RAYA_KERNEL_TC32_WS2 ||
+             (kernel_id == RAYA_KERNEL_TC32_STREAM && !stage_cycles)) {
     if (d->head_dim != 64)
       return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tensor-core kernel needs head_dim 64, got %lld",
                   static_cast<long long>(d->head_dim));
@@ -461,17 +494,27 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
       const long long resident = std::min<long long>(grid, ctx->sms);  // one CTA per SM walks the row tiles
       tc32::tc32_stream_fwd<<<static_cast<unsigned>(resident), tc32::kWsThreads, tc32::stream_smem_bytes(),
                               stream>>>(a, maps);
-    } else if (kernel_id == RAYA_KERNEL_TC32_WS)
-      tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 1>
-          <<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
-    else if (kernel_id == RAYA_KERNEL_TC32_WS2 && a.row_tiles == 4)  // a whole slice of four row tiles per CTA
-      tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 4>
-          <<<static_cast<unsigned>((grid + 3) / 4), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
-    else  // two 128-row tiles per CTA
-      tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 2>
-          <<<static_cast<unsigned>((grid + 1) / 2), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(a, maps);
+    } else {
+      // UNITS row tiles per CTA: 1 (kernel 34), 4 where a slice is four row
+      // tiles, else 2 (kernel 37); the stage-timing build where asked.
+      const int units = kernel_id == RAYA_KERNEL_TC32_WS ? 1 : a.row_tiles == 4 ? 4 : 2;
+      using WsFn = void (*)(AttnArgs, tc32::PipeMaps);
+      WsFn fn = nullptr;
+      if (units == 1)
+        fn = stage_cycles ? tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 1, true>
+                          : tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 1>;
+      else if (units == 4)
+        fn = stage_cycles ? tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 4, true>
+                          : tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 4>;
+      else
+        fn = stage_cycles ? tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 2, true>
+                          : tc32::tc32_ws_fwd<tiled64::kHeadMajor, false, 2>;
+      fn<<<static_cast<unsigned>((grid + units - 1) / units), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(
+          a, maps);
+    }
   } else if (stage_cycles) {
-    return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: stage timing needs a tiled kernel");
+    return fail(RAYA_ATTN_ERR_UNSUPPORTED,
+                "unsupported: stage timing needs a tiled kernel or the two-issuer tensor-core kernel");
   } else if (kernel_id == RAYA_KERNEL_ROWWISE) {
     const long long rows = static_cast<long long>(d->batch) * d->heads * d->seq;
     const long long want = (rows + rowwise::kWarps - 1) / rowwise::kWarps;
@@ -557,11 +600,26 @@ __global__ void __launch_bounds__(256) ffma_probe_kernel(float* sink, int iters,
 struct RopeFreq {
   float inv_freq[32];
 };
-__global__ void rope_table_kernel(float2* cs, int seq, const __grid_constant__ RopeFreq f) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= seq * 32) return;
-  const float angle = __fmul_rn(static_cast<float>(idx >> 5), f.inv_freq[idx & 31]);
-  cs[idx] = make_float2(cosf(angle), sinf(angle));
+// 64-bit element count and a grid-stride loop: seq * 32 passes 2^31 from
+// seq = 2^26 on, below the library's sequence limit.
+__global__ void rope_table_kernel(float2* cs, long long seq, const __grid_constant__ RopeFreq f) {
+  const long long n = seq * 32;
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < n;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float angle = __fmul_rn(static_cast<float>(idx >> 5), f.inv_freq[idx & 31]);
+    cs[idx] = make_float2(cosf(angle), sinf(angle));
+  }
+}
+
+// The rotary table's launch: enough CTAs for one element each, at most 32
+// per SM (the loop strides over the rest).
+raya_attn_status launch_rope_table(float2* cs, int64_t seq, const RopeFreq& f, int sms, cudaStream_t s) {
+  const long long n = static_cast<long long>(seq) * 32;
+  const long long blocks = std::max<long long>(1, std::min<long long>((n + 255) / 256, static_cast<long long>(sms) * 32));
+  rope_table_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(cs, seq, f);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rope table launch");
+  return RAYA_ATTN_OK;
 }
 
 // Failure-detection probe: one warp waits on an mbarrier that nothing ever
@@ -840,7 +898,6 @@ raya_attn_status raya_attn_forward_timed(const raya_attn_desc* desc, const float
   raya_attn_status st = check_shape(desc);
   if (st != RAYA_ATTN_OK) return st;
   if (!stage_cycles) return fail(RAYA_ATTN_ERR_SHAPE, "invalid shape: null stage counter buffer");
-  if (kernel_id == RAYA_KERNEL_AUTO) kernel_id = RAYA_KERNEL_TILED64;
   return launch(desc, q, k, v, out, valid_len, static_cast<cudaStream_t>(stream), kernel_id,
                 reinterpret_cast<unsigned long long*>(stage_cycles));
 }
@@ -938,10 +995,8 @@ raya_attn_status raya_attn_forward_packed(const raya_attn_desc* desc, const floa
     RopeFreq f;
     for (int i = 0; i < 32; ++i)  // ops.rs:120-122, in f32 with the C library's powf
       f.inv_freq[i] = 1.0f / powf(rope_theta, static_cast<float>(2 * i) / 64.0f);
-    const int n = static_cast<int>(desc->seq) * 32;
-    rope_table_kernel<<<(n + 255) / 256, 256, 0, s>>>(static_cast<float2*>(workspace), static_cast<int>(desc->seq), f);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "rope table launch");
+    st = launch_rope_table(static_cast<float2*>(workspace), desc->seq, f, ctx_dev->sms, s);
+    if (st != RAYA_ATTN_OK) return st;
   }
   return launch_packed(ctx_dev, desc, qkv, ctx, valid_len, rope ? static_cast<const float*>(workspace) : nullptr, s);
 }
@@ -984,10 +1039,8 @@ raya_attn_status raya_attn_forward_packed_noalloc(const raya_attn_desc* desc, co
     RopeFreq f;
     for (int i = 0; i < 32; ++i)  // ops.rs:120-122, in f32 with the C library's powf
       f.inv_freq[i] = 1.0f / powf(rope_theta, static_cast<float>(2 * i) / 64.0f);
-    const int n = static_cast<int>(desc->seq) * 32;
-    rope_table_kernel<<<(n + 255) / 256, 256, 0, s>>>(table, static_cast<int>(desc->seq), f);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "rope table launch");
+    st = launch_rope_table(table, desc->seq, f, ctx_dev->sms, s);
+    if (st != RAYA_ATTN_OK) return st;
   }
   return launch_packed(ctx_dev, desc, qkv, ctx, valid_len, rope ? reinterpret_cast<const float*>(table) : nullptr, s);
 }

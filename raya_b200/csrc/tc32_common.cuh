@@ -109,6 +109,23 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// D (+)= A B with both operands from shared-memory descriptors.
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+
+// K-major A (a 128-row q tile in two column halves of [128][32], 128-byte
+// swizzle): k-step s is column half s/4, byte 32*(s%4).
+__device__ __forceinline__ uint64_t q_desc(uint32_t base, int s) {
+  return smem_desc(base + (s >> 2) * (kBM * 128) + (s & 3) * 32, 16, 1024);
+}
+
 // K-major B (K hi/lo tile, 64 keys): k-step s is column half s/4, byte 32*(s%4).
 __device__ __forceinline__ uint64_t k_desc(uint32_t base, int s) {
   return smem_desc(base + (s >> 2) * (kBN * 128) + (s & 3) * 32, 16, 1024);

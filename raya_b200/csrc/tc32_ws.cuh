@@ -98,7 +98,19 @@ __device__ __forceinline__ void ws_rot(float& x, float& y, float c, float sn) {
 // after the other, each exactly as a CTA of its own (empty rings, barriers
 // set up again), so that only the CTA's launch, exit, tensor-memory
 // allocation and valid_len loads are shared between them.
-template <int LAYOUT, bool ROPE, int UNITS>
+// TIMED: the stage-timing build (the counterpart of the reference's
+// StageTimes, tiled/stages.rs:1-31): per unit, clock64 cycles added into
+// a.stage_cycles — [kStageQk] QK^T products in flight (issue to completion,
+// seen by the QK issuer, which in this build also waits for each QK's
+// completion: QK(j+1) needs the softmax's read of S(j) anyway), [kStageSoftmax]
+// one softmax warp's work per tile (S read to P stored), [kStagePv] PV
+// products in flight (the PV issuer waits for each PV's completion before
+// the next, a small perturbation), [kStageKWait] the QK issuer waiting for
+// K's operand split, [kStageVWait] the PV issuer waiting for P and V's split,
+// [kStageRefill] one split warp's operand preparation, [kStageTiles] key
+// tiles, [kStageTotal] thread 0's cycles from the unit's start to its output
+// store.  The stages overlap in time; read them as proportions.
+template <int LAYOUT, bool ROPE, int UNITS, bool TIMED = false>
 __global__ void __launch_bounds__(kWsThreads, 1)
     tc32_ws_fwd(const __grid_constant__ AttnArgs a, const __grid_constant__ PipeMaps maps) {
   static_assert(!ROPE || LAYOUT == tiled64::kPacked, "the rotation is fused into the packed layout only");
@@ -119,6 +131,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   };
   int valid_next = load_valid(blockIdx.x * UNITS);
   bool tmem_held = false;  // (uniform) tensor memory allocated by an earlier unit of this CTA
+  // Stage-timing accumulators of this thread (TIMED only).
+  unsigned long long c_a = 0, c_b = 0;
+  long long c_t0 = 0;
 #pragma unroll 1
   for (int uu = 0; uu < UNITS; ++uu) {
   const unsigned unit = blockIdx.x * UNITS + uu;
@@ -222,6 +237,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   tc_fence_after();
   if (tid == 0)
     for (int jj = 1; jj < kRawStages && jj < ntiles; ++jj) first_copy(jj);
+  if constexpr (TIMED) {
+    c_a = c_b = 0;
+    c_t0 = clock64();
+  }
   const uint32_t tmem = sm.tmem_base;
   volatile int* abort_flag = &sm.abort_flag;
 
@@ -289,6 +308,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
                                  a.timeout_cycles);
       if (__any_sync(0xffffffffu, !w)) { ok = false; break; }
       tc_fence_after();
+      long long c_s0 = 0;
+      if constexpr (TIMED) c_s0 = clock64();
       float sv[64];
       tmem_ld32(tmem + lane_off + kWsColS, sv);
       tmem_ld32(tmem + lane_off + kWsColS + 32, sv + 32);
@@ -357,6 +378,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&sm.p_ready2[pb]);
+      if constexpr (TIMED) c_a += static_cast<unsigned long long>(clock64() - c_s0);
     }
     float o[64];
 #pragma unroll
@@ -399,6 +421,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
                 tma_store_4d(&maps.o, stage + half * kBM * 32 + rb * 64 * 32, 32 * half, head, r0 + 64 * rb, b);
             }
         tma_store_commit_and_wait_read();
+        if constexpr (TIMED) {
+          atomicAdd(&a.stage_cycles[kStageSoftmax], c_a);
+          atomicAdd(&a.stage_cycles[kStageTiles], static_cast<unsigned long long>(ntiles));
+          atomicAdd(&a.stage_cycles[kStageTotal], static_cast<unsigned long long>(clock64() - c_t0));
+        }
       }
     }
   } else if (warp < 10) {
@@ -448,6 +475,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       if (w && j >= kLoStages) w = mbar_wait_bounded(&sm.k_free[s3], ph, abort_flag, a.status, a.timeout_cycles);
       if (w && j == 2) w = mbar_wait_bounded(&sm.q_ready, 0, abort_flag, a.status, a.timeout_cycles);  // q left lo stage 2
       if (bar_any(kSplitBarrier, kWsSplitThreads, !w)) break;
+      long long c_k0 = 0;
+      if constexpr (TIMED) c_k0 = clock64();
       const int nv = min(kBN, valid - (t_begin + j) * kBN);
       float4* kr = reinterpret_cast<float4*>(&sm.raw[s4][0][0][0][0]);
       float4* vr = reinterpret_cast<float4*>(&sm.raw[s4][1][0][0][0]);
@@ -494,12 +523,15 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
       mbar_arrive(&sm.k_ready[s3]);  // QK(j) may start
+      if constexpr (TIMED) c_a += static_cast<unsigned long long>(clock64() - c_k0);
       // V: V's lo stage and the raw stage of tile j-3 (PV(j-3) done).
       if (j >= kLoStages) {
         w = mbar_wait_bounded(&sm.v_free[s3], ph, abort_flag, a.status, a.timeout_cycles);
         if (w && st == 0 && j + 1 < ntiles) issue(j + 1);  // raw stage (j+1)%4 held tile j-3
       }
       if (bar_any(kSplitBarrier, kWsSplitThreads, !w)) break;
+      long long c_v0 = 0;
+      if constexpr (TIMED) c_v0 = clock64();
       {
         float4 x[kPer];
 #pragma unroll
@@ -520,15 +552,21 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&sm.v_ready[s3]);
+      if constexpr (TIMED) c_a += static_cast<unsigned long long>(clock64() - c_v0);
       bar_named(kSplitBarrier, kWsSplitThreads);
     }
+    if constexpr (TIMED)
+      if (st == 0) atomicAdd(&a.stage_cycles[kStageRefill], c_a);
   } else if (tid == kWsQkThread) {
     // ---------------- QK^T issuer ----------------
     bool ok = mbar_wait_bounded(&sm.q_ready, 0, abort_flag, a.status, a.timeout_cycles);
     for (int j = 0; ok && j < ntiles; ++j) {
       const int s3 = j % kLoStages;
+      long long c_w0 = 0;
+      if constexpr (TIMED) c_w0 = clock64();
       ok = mbar_wait_bounded(&sm.k_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u, abort_flag, a.status,
                              a.timeout_cycles);
+      if constexpr (TIMED) c_b += static_cast<unsigned long long>(clock64() - c_w0);
       if (ok && j >= 1)  // the softmax has read S(j-1)
         ok = mbar_wait_bounded(&sm.s_free[0], static_cast<uint32_t>(j - 1) & 1u, abort_flag, a.status,
                                a.timeout_cycles);
@@ -543,8 +581,18 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kWsColQl + 8 * k, k_desc(khi, k), kIdescQK, 1u);
 #pragma unroll
       for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kWsColQh + 8 * k, k_desc(khi, k), kIdescQK, 1u);
+      long long c_i0 = 0;
+      if constexpr (TIMED) c_i0 = clock64();
       commit(&sm.s_full[0], static_cast<uint32_t>(j) & 1u);
       if (j + kLoStages < ntiles) commit(&sm.k_free[s3], static_cast<uint32_t>(j / kLoStages) & 1u);
+      if constexpr (TIMED) {
+        ok = mbar_wait_bounded(&sm.s_full[0], static_cast<uint32_t>(j) & 1u, abort_flag, a.status, a.timeout_cycles);
+        c_a += static_cast<unsigned long long>(clock64() - c_i0);
+      }
+    }
+    if constexpr (TIMED) {
+      atomicAdd(&a.stage_cycles[kStageQk], c_a);
+      atomicAdd(&a.stage_cycles[kStageKWait], c_b);
     }
   } else if (tid == kWsPvThread) {
     // ---------------- PV issuer ----------------
@@ -552,10 +600,13 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     for (int j = 0; ok && j < ntiles; ++j) {
       const int s3 = j % kLoStages;
       const int pb = j & 1;
+      long long c_w0 = 0;
+      if constexpr (TIMED) c_w0 = clock64();
       ok = mbar_wait_bounded(&sm.p_ready2[pb], static_cast<uint32_t>(j >> 1) & 1u, abort_flag, a.status,
                              a.timeout_cycles) &&
            mbar_wait_bounded(&sm.v_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u, abort_flag, a.status,
                              a.timeout_cycles);
+      if constexpr (TIMED) c_b += static_cast<unsigned long long>(clock64() - c_w0);
       if (!ok) break;
       tc_fence_after();
       const uint32_t vh = smem_addr(&sm.raw[j & (kRawStages - 1)][1][0][0][0]);
@@ -568,8 +619,19 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       for (int k = 0; k < 8; ++k) mma_tf32_ts(d, apl + 8 * k, v_desc(vh, k), kIdescPV, 1u);
 #pragma unroll
       for (int k = 0; k < 8; ++k) mma_tf32_ts(d, aph + 8 * k, v_desc(vh, k), kIdescPV, 1u);
+      long long c_i0 = 0;
+      if constexpr (TIMED) c_i0 = clock64();
       commit(&sm.pv_done2[pb], static_cast<uint32_t>(j >> 1) & 1u);
       if (j + kLoStages < ntiles) commit(&sm.v_free[s3], static_cast<uint32_t>(j / kLoStages) & 1u);
+      if constexpr (TIMED) {
+        ok = mbar_wait_bounded(&sm.pv_done2[pb], static_cast<uint32_t>(j >> 1) & 1u, abort_flag, a.status,
+                               a.timeout_cycles);
+        c_a += static_cast<unsigned long long>(clock64() - c_i0);
+      }
+    }
+    if constexpr (TIMED) {
+      atomicAdd(&a.stage_cycles[kStagePv], c_a);
+      atomicAdd(&a.stage_cycles[kStageVWait], c_b);
     }
     if constexpr (UNITS > 1) {
       // The next unit sets the barriers up again: the one commit no other
