@@ -74,14 +74,14 @@ typedef struct {
 
 /* Kernel selection for raya_attn_forward_ex (tests and benchmarks). */
 typedef enum {
-  RAYA_KERNEL_AUTO = 0,     /* head_dim 64: RAYA_KERNEL_TC32_STREAM for block masks with
-                               halo 0 and block 128 or 256; the tensor-core kernel
+  RAYA_KERNEL_AUTO = 0,     /* head_dim 64: the tensor-core kernel
                                RAYA_KERNEL_TC32_WS for Full, windows of half width >= 64,
                                other blocks >= 128 and block masks with a halo whose
                                allowed keys fill >= half of a 128-row CTA's key span, in
                                its two-tile form RAYA_KERNEL_TC32_WS2 for such blocks
-                               below 128 with >= 1024 128-row tiles; else the tuned tiled
-                               kernel; other head_dims: rowwise */
+                               below 128 with >= 1024 128-row tiles and for blocks >= 128
+                               with >= 2048 tiles and at most 2048 keys per span; else the
+                               tuned tiled kernel; other head_dims: rowwise */
   RAYA_KERNEL_TILED64 = 1,  /* the tuned tiled variant for the mask and block (head_dim 64):
                                W4R16_P2 for block <= 64 and windows, W4R32_P2 for
                                block >= 128 and Full */
@@ -103,7 +103,9 @@ typedef enum {
   RAYA_KERNEL_TC32_WS = 34,
   /* The same pipeline in one resident CTA per SM that walks its 128-row
    * tiles back to back: each tile's q copy, key-tile splits and first QK^T
-   * overlap the previous tile's last key tiles and output store. */
+   * overlap the previous tile's last key tiles and output store.  On request
+   * only: it sums a tile's PV products in tensor memory, whose accumulation
+   * is biased toward zero (error grows with the key span). */
   RAYA_KERNEL_TC32_STREAM = 36,
   /* RAYA_KERNEL_TC32_WS with two 128-row tiles per CTA (four where a
    * (batch, head) slice is four row tiles, seq 385..512, so that a CTA runs

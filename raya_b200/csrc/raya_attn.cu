@@ -97,18 +97,28 @@ int tuned_tiled(const raya_attn_desc* d) {
 // for Full, windows of half width >= 64, blocks >= 128, and block masks with
 // a halo whose allowed keys per row, (2*halo + 1) * block, are at least half
 // of that span.  With halo 0 and blocks below 128 the 64-row tiles of the
-// tuned FFMA kernel waste less and win.  With halo 0 and blocks of 128 or
-// 256 every 128-row CTA has only 2 or 4 key tiles, and the persistent
-// variant, which overlaps one row tile's set-up and output with the previous
-// one's, wins (1.2x and 1.1x; from 512 on, or at halo >= 1, it loses).
+// tuned FFMA kernel waste less and win.  (The persistent kernel
+// RAYA_KERNEL_TC32_STREAM, faster on halo-0 blocks of 128 and 256, sums each
+// row tile's PV products in tensor memory, whose accumulation is biased
+// toward zero: with values of mean 1 its error reaches 8.5e-6 at block 128
+// and grows with the span, so it runs only on request.)
 constexpr long long kTwoTileMinTiles = 1024;
+constexpr long long kTwoTileMinTilesLong = 2048;
 int auto_kernel(const raya_attn_desc* d) {
   if (d->head_dim != 64) return RAYA_KERNEL_ROWWISE;
   if (d->mask == RAYA_MASK_FULL) return RAYA_KERNEL_TC32_WS;
   if (d->mask == RAYA_MASK_WINDOW) return d->window >= 64 ? RAYA_KERNEL_TC32_WS : tuned_tiled(d);
   const long long blk = d->block, halo = d->halo;
-  if (halo == 0 && blk % tc32::kBM == 0 && blk <= 2 * tc32::kBM) return RAYA_KERNEL_TC32_STREAM;
-  if (blk >= tc32::kBM) return RAYA_KERNEL_TC32_WS;
+  const long long tiles = d->batch * d->heads * ((d->seq + tc32::kBM - 1) / tc32::kBM);
+  if (blk >= tc32::kBM) {
+    // Two tiles per CTA pay off with many tiles (>= ~14 waves of 148 SMs)
+    // and key spans of at most 32 key tiles (c5: 138 against 134 TFLOP/s;
+    // Block3 at seq 2048 x 8: 147.7 against 141.6); with fewer tiles or
+    // longer spans the single-tile form wins (Block3 at seq 8192 x 1: 133.8
+    // against 129.3).
+    const long long span_keys = (2 * halo + 1) * blk;
+    return tiles >= kTwoTileMinTilesLong && span_keys <= 32 * tc32::kBN ? RAYA_KERNEL_TC32_WS2 : RAYA_KERNEL_TC32_WS;
+  }
   if (halo == 0) return tuned_tiled(d);
   const long long spanned = (tc32::kBM + blk - 1) / blk + (tc32::kBM % blk != 0 ? 1 : 0);
   const long long span = ((spanned + 2 * halo) * blk + tc32::kBN - 1) / tc32::kBN * tc32::kBN;
@@ -117,7 +127,6 @@ int auto_kernel(const raya_attn_desc* d) {
   // Short key ranges (blocks below 128) and many 128-row tiles (>= ~7 waves
   // of 148 SMs): two tiles per CTA share its launch and set-up (c2, c3-b64,
   // c4: +1.5-2.6%; with fewer tiles the halved CTA count costs more).
-  const long long tiles = d->batch * d->heads * ((d->seq + tc32::kBM - 1) / tc32::kBM);
   return tiles >= kTwoTileMinTiles ? RAYA_KERNEL_TC32_WS2 : RAYA_KERNEL_TC32_WS;
 }
 

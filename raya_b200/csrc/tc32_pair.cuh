@@ -35,6 +35,11 @@
 //               S has been read; q tiles are shared-memory operands.
 //   warp 11     PV issuer: PV(A, g), PV(B, g) into the units' partials once
 //               their P and V's lo part are ready.
+//               Both issuers run their loops on the whole warp and issue from
+//               one elected lane: a chain of MMAs into one accumulator then
+//               runs at ~64 cycles per MMA instead of ~120 (one lane in a
+//               divergent branch), and the two chains together keep the
+//               tensor core at its ~32.
 //
 // Shared memory (224 KB): both units' q tiles and their lo parts (the A
 // operands of QK^T, 128 KB), rings of two raw K and two raw V tiles (TMA
@@ -226,10 +231,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   int last_k = min(2, n) - 1, last_v = min(2, n) - 1;  // split thread 0: last tiles copied (the first two by thread 0)
   uint64_t* last_commit = nullptr;
   uint32_t last_commit_parity = 0;
-  auto commit = [&](uint64_t* bar, uint32_t parity) {
-    mma_commit(bar);
+  auto commit = [&](uint64_t* bar, uint32_t parity) {  // the issuing warps: one elected lane commits
+    mma_commit_e(bar);
     last_commit = bar;
     last_commit_parity = parity;
+  };
+  // A bounded wait whose outcome is the same on every lane of the warp.
+  auto warp_wait = [&](uint64_t* bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, a.status, a.timeout_cycles));
   };
   // Whether unit u uses union tile g, and the unit's own index of it.
   auto uses = [&](int u, int g) { return act[u] && g0 + g >= t0[u] && g0 + g < t1[u]; };
@@ -478,16 +487,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     if constexpr (TIMED)
       if (st == 0) atomicAdd(&a.stage_cycles[kStageRefill], c_split);
-  } else if (tid == kPairQkThread) {
-    // ---------------- QK^T issuer ----------------
+  } else if (warp == kPairQkThread / 32) {
+    // ---------------- QK^T issuer (the whole warp runs the loop; an elected lane issues) ----------------
     unsigned long long c_qk = 0, c_kw = 0;
     bool ok = true;
     for (int u = 0; u < 2 && ok; ++u)
-      if (act[u]) ok = mbar_wait_bounded(&sm.q_ready[u], 0, abort_flag, a.status, a.timeout_cycles);
+      if (act[u]) ok = warp_wait(&sm.q_ready[u], 0);
     for (int g = 0; ok && g < n; ++g) {
       long long c_w0 = 0;
       if constexpr (TIMED) c_w0 = clock64();
-      ok = mbar_wait_bounded(&sm.k_ready, static_cast<uint32_t>(g) & 1u, abort_flag, a.status, a.timeout_cycles);
+      ok = warp_wait(&sm.k_ready, static_cast<uint32_t>(g) & 1u);
       if constexpr (TIMED) c_kw += static_cast<unsigned long long>(clock64() - c_w0);
       if (!ok) break;
       tc_fence_after();
@@ -498,8 +507,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         if (!ok || !uses(u, g)) continue;
         const int j = g0 + g - t0[u];
         if (j > 0) {  // the softmax has read S(u, j-1)
-          ok = mbar_wait_bounded(&sm.s_free[u], static_cast<uint32_t>(j - 1) & 1u, abort_flag, a.status,
-                                 a.timeout_cycles);
+          ok = warp_wait(&sm.s_free[u], static_cast<uint32_t>(j - 1) & 1u);
           if (!ok) break;
           tc_fence_after();
         }
@@ -509,32 +517,33 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const uint32_t d = tmem + kPairColUnit * static_cast<uint32_t>(u) + kPairColS;
         // the correction products first, then hi x hi
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mma_tf32_ss(d, q_desc(qhi, k), k_desc(klo, k), kIdescQK, k > 0 ? 1u : 0u);
+        for (int k = 0; k < 8; ++k) mma_tf32_ss_e(d, q_desc(qhi, k), k_desc(klo, k), kIdescQK, k > 0 ? 1u : 0u);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mma_tf32_ss(d, q_desc(qlo, k), k_desc(khi, k), kIdescQK, 1u);
+        for (int k = 0; k < 8; ++k) mma_tf32_ss_e(d, q_desc(qlo, k), k_desc(khi, k), kIdescQK, 1u);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mma_tf32_ss(d, q_desc(qhi, k), k_desc(khi, k), kIdescQK, 1u);
+        for (int k = 0; k < 8; ++k) mma_tf32_ss_e(d, q_desc(qhi, k), k_desc(khi, k), kIdescQK, 1u);
         commit(&sm.s_full[u], static_cast<uint32_t>(j) & 1u);
         if constexpr (TIMED) {
-          ok = mbar_wait_bounded(&sm.s_full[u], static_cast<uint32_t>(j) & 1u, abort_flag, a.status,
-                                 a.timeout_cycles);
+          ok = warp_wait(&sm.s_full[u], static_cast<uint32_t>(j) & 1u);
           c_qk += static_cast<unsigned long long>(clock64() - c_i0);
         }
       }
       if (ok && g + 1 < n) commit(&sm.k_free, static_cast<uint32_t>(g) & 1u);
     }
     if constexpr (TIMED) {
-      atomicAdd(&a.stage_cycles[kStageQk], c_qk);
-      atomicAdd(&a.stage_cycles[kStageKWait], c_kw);
+      if (tid == kPairQkThread) {
+        atomicAdd(&a.stage_cycles[kStageQk], c_qk);
+        atomicAdd(&a.stage_cycles[kStageKWait], c_kw);
+      }
     }
-  } else if (tid == kPairPvThread) {
-    // ---------------- PV issuer ----------------
+  } else if (warp == kPairPvThread / 32) {
+    // ---------------- PV issuer (the whole warp runs the loop; an elected lane issues) ----------------
     unsigned long long c_pv = 0, c_vw = 0;
     bool ok = true;
     for (int g = 0; ok && g < n; ++g) {
       long long c_w0 = 0;
       if constexpr (TIMED) c_w0 = clock64();
-      ok = mbar_wait_bounded(&sm.v_ready, static_cast<uint32_t>(g) & 1u, abort_flag, a.status, a.timeout_cycles);
+      ok = warp_wait(&sm.v_ready, static_cast<uint32_t>(g) & 1u);
       if (!ok) break;
       tc_fence_after();
       const uint32_t vhi = smem_addr(&sm.vraw[g & 1][0][0][0]);
@@ -544,8 +553,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         if (!ok || !uses(u, g)) continue;
         const int j = g0 + g - t0[u];
         if constexpr (TIMED) c_w0 = clock64();
-        ok = mbar_wait_bounded(&sm.p_ready[u], static_cast<uint32_t>(j) & 1u, abort_flag, a.status,
-                               a.timeout_cycles);
+        ok = warp_wait(&sm.p_ready[u], static_cast<uint32_t>(j) & 1u);
         if constexpr (TIMED) c_vw += static_cast<unsigned long long>(clock64() - c_w0);
         if (!ok) break;
         tc_fence_after();
@@ -554,23 +562,24 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const uint32_t ub = tmem + kPairColUnit * static_cast<uint32_t>(u);
         const uint32_t d = ub + kPairColPv, aph = ub + kPairColPh, apl = ub + kPairColPl;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mma_tf32_ts(d, aph + 8 * k, v_desc(vlo, k), kIdescPV, k > 0 ? 1u : 0u);
+        for (int k = 0; k < 8; ++k) mma_tf32_ts_e(d, aph + 8 * k, v_desc(vlo, k), kIdescPV, k > 0 ? 1u : 0u);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mma_tf32_ts(d, apl + 8 * k, v_desc(vhi, k), kIdescPV, 1u);
+        for (int k = 0; k < 8; ++k) mma_tf32_ts_e(d, apl + 8 * k, v_desc(vhi, k), kIdescPV, 1u);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mma_tf32_ts(d, aph + 8 * k, v_desc(vhi, k), kIdescPV, 1u);
+        for (int k = 0; k < 8; ++k) mma_tf32_ts_e(d, aph + 8 * k, v_desc(vhi, k), kIdescPV, 1u);
         commit(&sm.pv_done[u], static_cast<uint32_t>(j) & 1u);
         if constexpr (TIMED) {
-          ok = mbar_wait_bounded(&sm.pv_done[u], static_cast<uint32_t>(j) & 1u, abort_flag, a.status,
-                                 a.timeout_cycles);
+          ok = warp_wait(&sm.pv_done[u], static_cast<uint32_t>(j) & 1u);
           c_pv += static_cast<unsigned long long>(clock64() - c_i0);
         }
       }
       if (ok && g + 1 < n) commit(&sm.v_free, static_cast<uint32_t>(g) & 1u);
     }
     if constexpr (TIMED) {
-      atomicAdd(&a.stage_cycles[kStagePv], c_pv);
-      atomicAdd(&a.stage_cycles[kStageVWait], c_vw);
+      if (tid == kPairPvThread) {
+        atomicAdd(&a.stage_cycles[kStagePv], c_pv);
+        atomicAdd(&a.stage_cycles[kStageVWait], c_vw);
+      }
     }
   }
   __syncwarp();

@@ -11,14 +11,18 @@
 //     in different warps sustain one per ~33.5, the tensor core's own rate
 //     (about 32).  So QK^T and PV are issued by separate warps, each with
 //     its own commit barriers, and the tensor core interleaves the streams.
-//   * O in tensor memory.  PV(j) accumulates straight into an O block of
-//     tensor memory (the first PV of the CTA overwrites it).  The softmax
-//     thread keeps a running log2-domain max m and rescales O (tcgen05.ld,
-//     multiply, tcgen05.st of its own row) only when a tile raises m by more
-//     than 2^8; otherwise it keeps the old m, so weights reach at most 256,
-//     and O and the row sum l stay on the same scale, which the final O / l
-//     removes.  Without o[64] in registers the softmax rows fit the register
-//     budget of a 384-thread block.
+//   * O summed in registers.  PV(j) goes into a fresh tensor-memory partial
+//     (a chain of 24 products); the softmax thread adds it into its O row in
+//     fp32 registers with round-to-nearest adds before PV(j+1) overwrites it.
+//     The tensor core's accumulation truncates toward zero (~0.5 ulp of the
+//     accumulator per MMA, measured): summing every tile's PV into one
+//     tensor-memory block put 1.5e-5 (6 tiles) to 1.6e-4 (128 tiles) of
+//     absolute error into outputs of size 1.  The softmax thread keeps a
+//     running log2-domain max m and rescales O only when a tile raises m by
+//     more than 2^8; otherwise it keeps the old m, so weights reach at most
+//     256, and O and the row sum l stay on the same scale, which the final
+//     O / l removes.  The softmax warp group takes 232 registers
+//     (setmaxnreg) for the O row next to a score row.
 //
 // Roles (384 threads):
 //   warps 0-3   softmax: one query row per thread (TMEM lane = row): q and
@@ -33,9 +37,12 @@
 //               j+1 (one copy for K and V).  So QK(j) never waits on a PV
 //               product.  (Issuing K's copy ahead of V's, on its own barrier,
 //               measured slower.)
-//   warp 10     QK issuer: QK(j) into S[j%2] once K's lo part is ready and
-//               S[j%2] has been read.
+//   warp 10     QK issuer: QK(j) into S once K's lo part is ready and S has
+//               been read.
 //   warp 11     PV issuer: PV(j) into O once P(j) and V's lo part are ready.
+//               Both issuers run their loops on the whole warp and issue from
+//               one elected lane (a chain of MMAs into one accumulator then
+//               runs at ~64 cycles per MMA instead of ~120).
 //
 // Tensor memory (512 columns): S [0,64), Q hi [64,128), Q lo [128,192),
 // P0 hi/lo [192,320), P1 hi/lo [320,448), O [448,512).  P is double-buffered
@@ -60,6 +67,12 @@ constexpr int kWsSplitThreads = 192;  // warps 4-9
 constexpr int kWsQkThread = 320;      // warp 10, lane 0
 constexpr int kWsPvThread = 352;      // warp 11, lane 0
 constexpr float kRescaleLog2 = 8.0f;  // rescale O when the running max grows by more than 2^8
+// Register split (setmaxnreg): the softmax warp group holds an O row (64
+// floats) next to a score row; the split and issue warp groups need few.
+// 232 + 136 + 136 = 504 = 3 warp groups x the 168 registers a thread of this
+// launch gets, so the increase never waits on the pool.
+constexpr int kWsSoftmaxRegs = 232, kWsOtherRegs = 136;
+static_assert(kWsSoftmaxRegs + 2 * kWsOtherRegs <= 3 * 168, "register split above the launch's allocation");
 constexpr int kSoftmaxBarrier = 2;    // named barrier of the softmax warps
 static_assert(kLoStages >= 3, "the q tile is staged in lo stage 2 before the split warps first use it");
 constexpr uint32_t kWsColS = 0, kWsColQh = 64, kWsColQl = 128, kWsColP = 192, kWsColO = 448;
@@ -248,12 +261,20 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   int last_tma_tile = min(kRawStages, ntiles) - 1;  // split thread 0: last tile copied (the first four by thread 0)
   uint64_t* last_commit = nullptr;
   uint32_t last_commit_parity = 0;
-  auto commit = [&](uint64_t* bar, uint32_t parity) {
-    mma_commit(bar);
+  auto commit = [&](uint64_t* bar, uint32_t parity) {  // the issuing warps: one elected lane commits
+    mma_commit_e(bar);
     last_commit = bar;
     last_commit_parity = parity;
   };
+  // A bounded wait whose outcome is the same on every lane of the warp.
+  auto warp_wait = [&](uint64_t* bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, a.status, a.timeout_cycles));
+  };
 
+  if (warp < 4)
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kWsSoftmaxRegs));
+  else
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWsOtherRegs));
   if (warp < 4) {
     // ---------------- softmax warpgroup ----------------
     const int row = r0 + tid;
@@ -300,6 +321,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     }
 
     float m_used = -INFINITY, lsum = 0.f;
+    float o[64];  // this row of O, summed in fp32 registers (round to nearest)
+#pragma unroll
+    for (int c = 0; c < 64; ++c) o[c] = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int pb = j & 1;  // P buffer
@@ -345,22 +369,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
       lsum = fmaf(lsum, alpha, rs);
 
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        // O row *= alpha (lanes with alpha 1 are unchanged), once PV(j-1) is
-        // complete (O then holds tiles 0..j-1).
-        w = mbar_wait_bounded(&sm.pv_done2[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag,
-                              a.status, a.timeout_cycles);
-        if (__any_sync(0xffffffffu, !w)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 64; c += 32) {
-          float t[32];
-          tmem_ld32(tmem + lane_off + kWsColO + c, t);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) t[i] *= alpha;
-          tmem_st32(tmem + lane_off + kWsColO + c, t);
-        }
-      }
       if (j >= 2) {  // P buffer pb is free once PV(j-2) is complete
         w = mbar_wait_bounded(&sm.pv_done2[pb], static_cast<uint32_t>((j - 2) >> 1) & 1u, abort_flag, a.status,
                               a.timeout_cycles);
@@ -375,21 +383,44 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       for (int c = 0; c < 64; ++c) sv[c] = tf32_lo(sv[c]);
       tmem_st32(ph + 64, sv);
       tmem_st32(ph + 96, sv + 32);
+      if (j > 0) {
+        // O = (O + PV partial of tile j-1) * alpha, both at the previous
+        // scale, once PV(j-1) is complete; PV(j) then overwrites the partial.
+        w = mbar_wait_bounded(&sm.pv_done2[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, abort_flag,
+                              a.status, a.timeout_cycles);
+        if (__any_sync(0xffffffffu, !w)) { ok = false; break; }
+        tc_fence_after();
+        const bool rescale = __any_sync(0xffffffffu, alpha != 1.f);
+#pragma unroll
+        for (int c = 0; c < 64; c += 32) {
+          float t[32];
+          tmem_ld32(tmem + lane_off + kWsColO + c, t);
+          if (rescale) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[c + i] = __fmul_rn(__fadd_rn(o[c + i], t[i]), alpha);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[c + i] = __fadd_rn(o[c + i], t[i]);
+          }
+        }
+      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&sm.p_ready2[pb]);
       if constexpr (TIMED) c_a += static_cast<unsigned long long>(clock64() - c_s0);
     }
-    float o[64];
-#pragma unroll
-    for (int c = 0; c < 64; ++c) o[c] = 0.f;
-    if (ok) {
+    if (ok) {  // the last tile's partial
       const bool w = mbar_wait_bounded(&sm.pv_done2[(ntiles - 1) & 1], static_cast<uint32_t>((ntiles - 1) >> 1) & 1u,
                                        abort_flag, a.status, a.timeout_cycles);
       if (!__any_sync(0xffffffffu, !w)) {
         tc_fence_after();
-        tmem_ld32(tmem + lane_off + kWsColO, o);
-        tmem_ld32(tmem + lane_off + kWsColO + 32, o + 32);
+#pragma unroll
+        for (int c = 0; c < 64; c += 32) {
+          float t[32];
+          tmem_ld32(tmem + lane_off + kWsColO + c, t);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[c + i] = __fadd_rn(o[c + i], t[i]);
+        }
       }
     }
     // This row, normalised (+0.0f past valid_len), staged in shared memory
@@ -557,55 +588,53 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     }
     if constexpr (TIMED)
       if (st == 0) atomicAdd(&a.stage_cycles[kStageRefill], c_a);
-  } else if (tid == kWsQkThread) {
-    // ---------------- QK^T issuer ----------------
-    bool ok = mbar_wait_bounded(&sm.q_ready, 0, abort_flag, a.status, a.timeout_cycles);
+  } else if (warp == kWsQkThread / 32) {
+    // ---------------- QK^T issuer (the whole warp runs the loop; an elected lane issues) ----------------
+    bool ok = warp_wait(&sm.q_ready, 0);
     for (int j = 0; ok && j < ntiles; ++j) {
       const int s3 = j % kLoStages;
       long long c_w0 = 0;
       if constexpr (TIMED) c_w0 = clock64();
-      ok = mbar_wait_bounded(&sm.k_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u, abort_flag, a.status,
-                             a.timeout_cycles);
+      ok = warp_wait(&sm.k_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u);
       if constexpr (TIMED) c_b += static_cast<unsigned long long>(clock64() - c_w0);
       if (ok && j >= 1)  // the softmax has read S(j-1)
-        ok = mbar_wait_bounded(&sm.s_free[0], static_cast<uint32_t>(j - 1) & 1u, abort_flag, a.status,
-                               a.timeout_cycles);
+        ok = warp_wait(&sm.s_free[0], static_cast<uint32_t>(j - 1) & 1u);
       if (!ok) break;
       tc_fence_after();
       const uint32_t khi = smem_addr(&sm.raw[j & (kRawStages - 1)][0][0][0][0]);
       const uint32_t klo = smem_addr(&sm.lo[s3][0][0][0][0]);
       const uint32_t d = tmem + kWsColS;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kWsColQh + 8 * k, k_desc(klo, k), kIdescQK, k > 0 ? 1u : 0u);
+      for (int k = 0; k < 8; ++k) mma_tf32_ts_e(d, tmem + kWsColQh + 8 * k, k_desc(klo, k), kIdescQK, k > 0 ? 1u : 0u);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kWsColQl + 8 * k, k_desc(khi, k), kIdescQK, 1u);
+      for (int k = 0; k < 8; ++k) mma_tf32_ts_e(d, tmem + kWsColQl + 8 * k, k_desc(khi, k), kIdescQK, 1u);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, tmem + kWsColQh + 8 * k, k_desc(khi, k), kIdescQK, 1u);
+      for (int k = 0; k < 8; ++k) mma_tf32_ts_e(d, tmem + kWsColQh + 8 * k, k_desc(khi, k), kIdescQK, 1u);
       long long c_i0 = 0;
       if constexpr (TIMED) c_i0 = clock64();
       commit(&sm.s_full[0], static_cast<uint32_t>(j) & 1u);
       if (j + kLoStages < ntiles) commit(&sm.k_free[s3], static_cast<uint32_t>(j / kLoStages) & 1u);
       if constexpr (TIMED) {
-        ok = mbar_wait_bounded(&sm.s_full[0], static_cast<uint32_t>(j) & 1u, abort_flag, a.status, a.timeout_cycles);
+        ok = warp_wait(&sm.s_full[0], static_cast<uint32_t>(j) & 1u);
         c_a += static_cast<unsigned long long>(clock64() - c_i0);
       }
     }
     if constexpr (TIMED) {
-      atomicAdd(&a.stage_cycles[kStageQk], c_a);
-      atomicAdd(&a.stage_cycles[kStageKWait], c_b);
+      if (tid == kWsQkThread) {
+        atomicAdd(&a.stage_cycles[kStageQk], c_a);
+        atomicAdd(&a.stage_cycles[kStageKWait], c_b);
+      }
     }
-  } else if (tid == kWsPvThread) {
-    // ---------------- PV issuer ----------------
+  } else if (warp == kWsPvThread / 32) {
+    // ---------------- PV issuer (the whole warp runs the loop; an elected lane issues) ----------------
     bool ok = true;
     for (int j = 0; ok && j < ntiles; ++j) {
       const int s3 = j % kLoStages;
       const int pb = j & 1;
       long long c_w0 = 0;
       if constexpr (TIMED) c_w0 = clock64();
-      ok = mbar_wait_bounded(&sm.p_ready2[pb], static_cast<uint32_t>(j >> 1) & 1u, abort_flag, a.status,
-                             a.timeout_cycles) &&
-           mbar_wait_bounded(&sm.v_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u, abort_flag, a.status,
-                             a.timeout_cycles);
+      ok = warp_wait(&sm.p_ready2[pb], static_cast<uint32_t>(j >> 1) & 1u) &&
+           warp_wait(&sm.v_ready[s3], static_cast<uint32_t>(j / kLoStages) & 1u);
       if constexpr (TIMED) c_b += static_cast<unsigned long long>(clock64() - c_w0);
       if (!ok) break;
       tc_fence_after();
@@ -613,32 +642,30 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const uint32_t vl = smem_addr(&sm.lo[s3][1][0][0][0]);
       const uint32_t d = tmem + kWsColO, aph = tmem + ws_col_ph(pb), apl = aph + 64;
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        mma_tf32_ts(d, aph + 8 * k, v_desc(vl, k), kIdescPV, (j > 0 || k > 0) ? 1u : 0u);
+      for (int k = 0; k < 8; ++k) mma_tf32_ts_e(d, aph + 8 * k, v_desc(vl, k), kIdescPV, k > 0 ? 1u : 0u);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, apl + 8 * k, v_desc(vh, k), kIdescPV, 1u);
+      for (int k = 0; k < 8; ++k) mma_tf32_ts_e(d, apl + 8 * k, v_desc(vh, k), kIdescPV, 1u);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mma_tf32_ts(d, aph + 8 * k, v_desc(vh, k), kIdescPV, 1u);
+      for (int k = 0; k < 8; ++k) mma_tf32_ts_e(d, aph + 8 * k, v_desc(vh, k), kIdescPV, 1u);
       long long c_i0 = 0;
       if constexpr (TIMED) c_i0 = clock64();
       commit(&sm.pv_done2[pb], static_cast<uint32_t>(j >> 1) & 1u);
       if (j + kLoStages < ntiles) commit(&sm.v_free[s3], static_cast<uint32_t>(j / kLoStages) & 1u);
       if constexpr (TIMED) {
-        ok = mbar_wait_bounded(&sm.pv_done2[pb], static_cast<uint32_t>(j >> 1) & 1u, abort_flag, a.status,
-                               a.timeout_cycles);
+        ok = warp_wait(&sm.pv_done2[pb], static_cast<uint32_t>(j >> 1) & 1u);
         c_a += static_cast<unsigned long long>(clock64() - c_i0);
       }
     }
     if constexpr (TIMED) {
-      atomicAdd(&a.stage_cycles[kStagePv], c_a);
-      atomicAdd(&a.stage_cycles[kStageVWait], c_b);
+      if (tid == kWsPvThread) {
+        atomicAdd(&a.stage_cycles[kStagePv], c_a);
+        atomicAdd(&a.stage_cycles[kStageVWait], c_b);
+      }
     }
     if constexpr (UNITS > 1) {
       // The next unit sets the barriers up again: the one commit no other
       // thread waits for (PV of tile ntiles-2) must have arrived first.
-      if (ok && ntiles >= 2)
-        mbar_wait_bounded(&sm.pv_done2[(ntiles - 2) & 1], static_cast<uint32_t>((ntiles - 2) >> 1) & 1u, abort_flag,
-                          a.status, a.timeout_cycles);
+      if (ok && ntiles >= 2) warp_wait(&sm.pv_done2[(ntiles - 2) & 1], static_cast<uint32_t>((ntiles - 2) >> 1) & 1u);
     }
   }
   __syncwarp();

@@ -165,8 +165,8 @@ def test_packed_call_validates_on_the_host():
 
 def test_two_tile_form_for_short_blocks_with_many_tiles():
     """Blocks below 128 with a halo and >= 1024 128-row tiles (c2: 32 x 12 x 8) run the two-tile
-    form of the tensor-core kernel, in the packed layout too unless it rotates; with fewer tiles or
-    blocks of 128, the one-tile form."""
+    form of the tensor-core kernel, in the packed layout too unless it rotates; with fewer tiles,
+    the one-tile form."""
     params = rb.AttnParams.new(rb.Mask.block(1), [1024] * 32, 64, block=64)
     c2 = _shape(heads=12, seq=1024, d=64, batch=32)
     assert rb.kernel_for(c2, params) == rb._lib.KERNEL_TC32_WS2
@@ -175,14 +175,17 @@ def test_two_tile_form_for_short_blocks_with_many_tiles():
     assert rb.kernel_for(c2, params, rope=True) == rb._lib.KERNEL_TC32_WS2  # head-major: no rotation
     small = rb.AttnParams.new(rb.Mask.block(1), [1024] * 2, 64, block=64)
     assert rb.kernel_for(_shape(heads=12, seq=1024, d=64, batch=2), small) == rb._lib.KERNEL_TC32_WS
+    # blocks of 128: the two-tile form from 2048 tiles on (here 3072), the one-tile form below
     b128 = rb.AttnParams.new(rb.Mask.block(1), [1024] * 32, 64, block=128)
-    assert rb.kernel_for(_shape(heads=12, seq=1024, d=64, batch=32), b128) == rb._lib.KERNEL_TC32_WS
+    assert rb.kernel_for(_shape(heads=12, seq=1024, d=64, batch=32), b128) == rb._lib.KERNEL_TC32_WS2
+    b128s = rb.AttnParams.new(rb.Mask.block(1), [1024] * 4, 64, block=128)
+    assert rb.kernel_for(_shape(heads=12, seq=1024, d=64, batch=4), b128s) == rb._lib.KERNEL_TC32_WS
 
 
 @pytest.mark.parametrize("mask,block,expect_tc", [
     (rb.Mask.block(1), 128, True),    # Block3: every allowed key of a 128-row span
-    (rb.Mask.block(0), 256, "stream"),  # halo 0, 2-4 key tiles per 128-row tile: the persistent kernel
-    (rb.Mask.block(0), 128, "stream"),
+    (rb.Mask.block(0), 256, True),    # halo 0, 2-4 key tiles per 128-row tile (the persistent kernel: on request)
+    (rb.Mask.block(0), 128, True),
     (rb.Mask.block(0), 512, True),
     (rb.Mask.block(0), 192, True),
     (rb.Mask.block(2), 64, True),     # 320 of 384 span keys allowed per row
@@ -197,8 +200,7 @@ def test_two_tile_form_for_short_blocks_with_many_tiles():
 ])
 def test_automatic_kernel_choice(mask, block, expect_tc):
     """The host-side rule behind RAYA_KERNEL_AUTO: the tensor-core kernel
-    (RAYA_KERNEL_TC32_WS) where enough of a 128-row CTA's key span is allowed, its persistent
-    variant (RAYA_KERNEL_TC32_STREAM) for halo 0 with blocks of 128 or 256, the tuned FFMA
+    (RAYA_KERNEL_TC32_WS) where enough of a 128-row CTA's key span is allowed, the tuned FFMA
     kernel else, rowwise for head_dim != 64 (no device work involved)."""
     shape = _shape(heads=2, seq=1024, d=64)
     params = rb.AttnParams.new(mask, 1024, 64, block=block)
@@ -276,3 +278,15 @@ def test_no_cpu_fallback_when_the_library_is_missing(tmp_path):
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True)
     assert out.returncode == 0, out.stderr
     assert "raised:" in out.stdout and "no fallback" in out.stdout
+
+
+def test_automatic_choice_two_tile_form_for_many_long_block_tiles():
+    """Blocks of 128 or more with a halo take the two-tile form (kernel 37)
+    when there are >= 2048 row tiles and the span is at most 2048 keys (c5's
+    shape), the single-tile form otherwise."""
+    params = lambda b: rb.AttnParams.new(rb.Mask.block(1), 8192, 64, block=b)
+    c5 = _shape(heads=16, seq=8192, d=64, batch=256)
+    assert rb.kernel_for(c5, params(128)) == rb.KERNEL_TC32_WS2
+    one = _shape(heads=16, seq=8192, d=64, batch=1)  # 1024 tiles
+    assert rb.kernel_for(one, params(128)) == rb.KERNEL_TC32_WS
+    assert rb.kernel_for(c5, params(1024)) == rb.KERNEL_TC32_WS  # 3072 keys per span
