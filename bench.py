@@ -54,8 +54,7 @@ def parse():
     ap.add_argument("--no-gather", action="store_true", help="skip the timed output gather to rank 0 (N > 1)")
     ap.add_argument("--gather-reps", type=int, default=3)
     ap.add_argument("--halo", type=int, default=1)
-    ap.add_argument("--kernel", type=int, default=0, help="0 auto, 1 tiled64, 2 rowwise, 34 tc32_ws, 36 tc32_stream, 37 tc32_ws two-tile, 38 tc32_pair "
-                         "(3xTF32 tensor cores)")
+    ap.add_argument("--kernel", type=int, default=0, help="0 auto, 1 tiled64, 2 rowwise, 34 tc32_ws, 37 tc32_ws two-tile (3xTF32 tensor cores)")
     ap.add_argument("--e2e-steps", type=int, default=3,
                     help="timed host-buffer calls (each copies the step's inputs in and its output out)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -258,18 +257,12 @@ def kernel_label(rb, chosen, shape, packed) -> str:
     if chosen == rb.KERNEL_ROWWISE:
         return "rowwise (raya_b200/csrc/rowwise.cuh)"
     if chosen == rb.KERNEL_TC32_WS:
-        return ("tc32_ws, two MMA-issuing warps, O in tensor memory, 3xTF32 tcgen05 (raya_b200/csrc/tc32_ws.cuh), "
-                "kernel id 34")
+        return ("tc32_ws, two MMA-issuing warps, PV summed in fp32 registers, 3xTF32 tcgen05 "
+                "(raya_b200/csrc/tc32_ws.cuh), kernel id 34")
     if chosen == rb.KERNEL_TC32_WS2:
         return (("tc32_ws with four 128-row tiles (a whole slice) per CTA" if (shape.seq + 127) // 128 == 4
                  and not packed else "tc32_ws with two 128-row tiles per CTA")
                 + " (raya_b200/csrc/tc32_ws.cuh), kernel id 37")
-    if chosen == rb.KERNEL_TC32_PAIR:
-        return ("tc32_pair, two 128-row tiles per CTA sharing one K/V stream, PV summed in fp32 registers, "
-                "3xTF32 tcgen05 (raya_b200/csrc/tc32_pair.cuh), kernel id 38")
-    if chosen == rb.KERNEL_TC32_STREAM:
-        return ("tc32_stream, one resident CTA per SM streaming its row tiles, 3xTF32 tcgen05 "
-                "(raya_b200/csrc/tc32_stream.cuh), kernel id 36")
     return f"tiled64 (raya_b200/csrc/tiled64.cuh), kernel id {chosen}"
 
 
@@ -337,7 +330,7 @@ def run_b200(args) -> None:
     chosen = (rb.kernel_for(shape, params, packed=args.packed, rope=args.rope_theta > 0)
               if args.kernel == rb.KERNEL_AUTO else args.kernel) if shape.batch > 0 else rb.KERNEL_AUTO
     tiled_ids = set(rb._lib.KERNEL_TILED64_VARIANTS.values()) | {rb.KERNEL_TILED64}
-    TENSOR_KERNELS = (rb.KERNEL_TC32_WS, rb.KERNEL_TC32_STREAM, rb.KERNEL_TC32_WS2, rb.KERNEL_TC32_PAIR)
+    TENSOR_KERNELS = (rb.KERNEL_TC32_WS, rb.KERNEL_TC32_WS2)
     stream = torch.cuda.current_stream(dev)
 
     # Live FFMA peak of this GPU (the fp32-equivalent denominator: no FP32
@@ -479,9 +472,7 @@ def run_b200(args) -> None:
     # Stage proportions of one extra, instrumented launch (the reference
     # bench's "stages" field, benches/local_attention.rs:127-130,155-157).
     stages = None
-    if not args.packed and shape.batch > 0 and (chosen in tiled_ids or chosen in (rb.KERNEL_TC32_WS,
-                                                                                  rb.KERNEL_TC32_WS2,
-                                                                                  rb.KERNEL_TC32_PAIR)):
+    if not args.packed and shape.batch > 0 and (chosen in tiled_ids or chosen in TENSOR_KERNELS):
         st = rb.stage_times(shape, params, q, k, v, out, valid_len=dvalid, kernel=chosen)
         stages = {key: round(val, 2) for key, val in st.items() if key.endswith("pct")}
 

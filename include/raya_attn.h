@@ -97,28 +97,16 @@ typedef enum {
    * as itself (read as TF32) and as its remainder, three products per tile,
    * fp32-level accuracy; head_dim 64, 128-row tiles.  Warp-specialised: a
    * split warp group prepares the K/V operand stages, QK^T and PV are issued
-   * by two warps (one issuing thread sustains only ~2/3 of the tensor core's
-   * rate at N = 64), and the O accumulator lives in tensor memory, rescaled
-   * only when a row's max grows by more than 2^8. */
+   * by two warps, and each key tile's PV product is added into the O rows in
+   * fp32 registers (the tensor core's own accumulation truncates toward
+   * zero, which over many tiles would exceed the parity bar). */
   RAYA_KERNEL_TC32_WS = 34,
-  /* The same pipeline in one resident CTA per SM that walks its 128-row
-   * tiles back to back: each tile's q copy, key-tile splits and first QK^T
-   * overlap the previous tile's last key tiles and output store.  On request
-   * only: it sums a tile's PV products in tensor memory, whose accumulation
-   * is biased toward zero (error grows with the key span). */
-  RAYA_KERNEL_TC32_STREAM = 36,
   /* RAYA_KERNEL_TC32_WS with two 128-row tiles per CTA (four where a
    * (batch, head) slice is four row tiles, seq 385..512, so that a CTA runs
    * the whole slice; head-major layout), one after the other, each run as a
    * CTA of its own (sharing only the CTA's launch, tensor-memory allocation
    * and valid_len loads). */
-  RAYA_KERNEL_TC32_WS2 = 37,
-  /* Two consecutive 128-row tiles of a slice per CTA sharing one K/V stream
-   * (each K/V tile loaded and split once for both), two softmax warp groups
-   * side by side, q tiles as shared-memory operands, and each key tile's PV
-   * product added into the O rows in fp32 registers (the tensor core's
-   * accumulation in tensor memory is biased toward zero over long chains). */
-  RAYA_KERNEL_TC32_PAIR = 38
+  RAYA_KERNEL_TC32_WS2 = 37
 } raya_kernel_id;
 
 /* Argument checks of validate (attention.rs:128-170), extended to the batch
@@ -224,9 +212,8 @@ raya_attn_status raya_attn_forward_packed_noalloc(const raya_attn_desc* desc, co
  * (tiled/mod.rs:60-126, tiled/stages.rs:1-31): raya_attn_forward_ex whose
  * kernel reads clock64 around each stage and adds the cycle counts into
  * stage_cycles, a DEVICE array of 8 uint64 that the caller zeroes.
- * kernel_id: RAYA_KERNEL_AUTO (the automatic choice; RAYA_KERNEL_TC32_WS
- * where that is RAYA_KERNEL_TC32_STREAM), TILED64 or a TILED64_* variant, or
- * RAYA_KERNEL_TC32_WS / RAYA_KERNEL_TC32_WS2.
+ * kernel_id: RAYA_KERNEL_AUTO (the automatic choice), TILED64 or a
+ * TILED64_* variant, or RAYA_KERNEL_TC32_WS / RAYA_KERNEL_TC32_WS2.
  * Tiled kernels (warp cycles summed over warps): [0] QK^T, [1] softmax,
  * [2] P.V, [3] K-tile wait, [4] V-tile wait, [5] next-tile refill,
  * [6] warp-tiles processed, [7] total cycles.

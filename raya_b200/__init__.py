@@ -22,8 +22,7 @@ _FROM_ATTENTION = (
     "sync_status", "validate", "work",
 )
 _FROM_LIB = (
-    "KERNEL_AUTO", "KERNEL_ROWWISE", "KERNEL_TC32_PAIR", "KERNEL_TC32_STREAM", "KERNEL_TC32_WS", "KERNEL_TC32_WS2",
-    "KERNEL_TILED64",
+    "KERNEL_AUTO", "KERNEL_ROWWISE", "KERNEL_TC32_WS", "KERNEL_TC32_WS2", "KERNEL_TILED64",
     "LIB_PATH",
 )
 

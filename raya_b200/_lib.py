@@ -16,9 +16,7 @@ OK, ERR_SHAPE, ERR_LENGTH, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_NCCL = ra
 MASK_BLOCK, MASK_WINDOW, MASK_FULL = 0, 1, 2
 KERNEL_AUTO, KERNEL_TILED64, KERNEL_ROWWISE = 0, 1, 2
 KERNEL_TC32_WS = 34
-KERNEL_TC32_STREAM = 36
 KERNEL_TC32_WS2 = 37
-KERNEL_TC32_PAIR = 38
 KERNEL_TILED64_VARIANTS = {"w4r32": 16, "w4r16": 19, "w4r16p2": 20, "w4r32p2": 21}
 
 # Every symbol include/raya_attn.h declares (checked by the ABI test).

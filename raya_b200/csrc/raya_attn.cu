@@ -21,9 +21,7 @@
 #include "common.cuh"
 #include "rowwise.cuh"
 #include "tc32_common.cuh"
-#include "tc32_pair.cuh"
 #include "tc32_ws.cuh"
-#include "tc32_stream.cuh"
 #include "tiled64.cuh"
 
 namespace raya {
@@ -97,11 +95,7 @@ int tuned_tiled(const raya_attn_desc* d) {
 // for Full, windows of half width >= 64, blocks >= 128, and block masks with
 // a halo whose allowed keys per row, (2*halo + 1) * block, are at least half
 // of that span.  With halo 0 and blocks below 128 the 64-row tiles of the
-// tuned FFMA kernel waste less and win.  (The persistent kernel
-// RAYA_KERNEL_TC32_STREAM, faster on halo-0 blocks of 128 and 256, sums each
-// row tile's PV products in tensor memory, whose accumulation is biased
-// toward zero: with values of mean 1 its error reaches 8.5e-6 at block 128
-// and grows with the span, so it runs only on request.)
+// tuned FFMA kernel waste less and win.
 constexpr long long kTwoTileMinTiles = 1024;
 constexpr long long kTwoTileMinTilesLong = 2048;
 int auto_kernel(const raya_attn_desc* d) {
@@ -134,14 +128,11 @@ int auto_kernel(const raya_attn_desc* d) {
 // packed layout where the automatic choice is a tensor-core kernel, else the
 // tuned tiled kernel.  Its two-tile form where that is the choice (two tiles
 // per CTA in this layout), except with the rotation (whose two-tile form
-// spills registers and measured slower);
-// the persistent kernel has no packed form.
+// spills registers and measured slower).
 int packed_kernel(const raya_attn_desc* d, bool rope) {
   const int id = auto_kernel(d);
   if (id == RAYA_KERNEL_TC32_WS2 && !rope) return id;
-  return id == RAYA_KERNEL_TC32_WS || id == RAYA_KERNEL_TC32_WS2 || id == RAYA_KERNEL_TC32_STREAM
-             ? RAYA_KERNEL_TC32_WS
-             : tuned_tiled(d);
+  return id == RAYA_KERNEL_TC32_WS || id == RAYA_KERNEL_TC32_WS2 ? RAYA_KERNEL_TC32_WS : tuned_tiled(d);
 }
 
 // Device status word: bit 0 = a bounded wait gave up.  One per device that
@@ -234,14 +225,6 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
                                static_cast<int>(tc32::pipe_smem_bytes()));
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_ws smem)");
     }
-    for (auto fn : {tc32::tc32_pair_fwd<false>, tc32::tc32_pair_fwd<true>}) {
-      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(tc32::pair_smem_bytes()));
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_pair smem)");
-    }
-    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(tc32::tc32_stream_fwd),
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(tc32::stream_smem_bytes()));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_stream smem)");
     for (const PackedVariant& pv : kPacked) {
       for (auto fn : {pv.plain, pv.rope}) {
         e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
@@ -431,12 +414,7 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
   AttnArgs a = make_args(d, q, k, v, out, valid_len, ctx->status);
   a.stage_cycles = stage_cycles;
 
-  if (kernel_id == RAYA_KERNEL_AUTO) {
-    kernel_id = auto_kernel(d);
-    // stage timing of the automatic choice, or of the two-issuer kernel where
-    // that is the persistent one (which has no timed build)
-    if (stage_cycles && kernel_id == RAYA_KERNEL_TC32_STREAM) kernel_id = RAYA_KERNEL_TC32_WS;
-  }
+  if (kernel_id == RAYA_KERNEL_AUTO) kernel_id = auto_kernel(d);
   if (kernel_id == RAYA_KERNEL_TILED64) kernel_id = tuned_tiled(d);
   const TiledVariant* tv = nullptr;
   for (const TiledVariant& t : kTiled)
@@ -458,29 +436,7 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     if (st != RAYA_ATTN_OK) return st;
     auto fn = stage_cycles ? tv->timed : tv->fn;
     fn<<<static_cast<unsigned>(grid), tv->warps * 32, tv->smem, stream>>>(a, maps);
-  } else if (kernel_id == RAYA_KERNEL_TC32_PAIR) {
-    if (d->head_dim != 64)
-      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tensor-core kernel needs head_dim 64, got %lld",
-                  static_cast<long long>(d->head_dim));
-    a.row_tiles = static_cast<int>((d->seq + 2 * tc32::kBM - 1) / (2 * tc32::kBM));  // 256-row pairs per slice
-    const long long grid = static_cast<long long>(d->batch) * d->heads * a.row_tiles;
-    if (grid > 0x7fffffffll)
-      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
-    const uint64_t rows = static_cast<uint64_t>(d->batch) * d->heads * d->seq;
-    if (rows > 0x7fffffffull)
-      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %llu rows exceed the tensor-map row limit",
-                  static_cast<unsigned long long>(rows));
-    tc32::PipeMaps maps;
-    raya_attn_status st = encode_rows64(&maps.k, k, rows, tc32::kBN);
-    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tc32::kBN, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
-    if (st == RAYA_ATTN_OK)
-      st = encode_slices3d(&maps.o, out, static_cast<uint64_t>(d->batch) * d->heads, static_cast<uint64_t>(d->seq));
-    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.q, q, rows, tc32::kBN);
-    if (st != RAYA_ATTN_OK) return st;
-    (stage_cycles ? tc32::tc32_pair_fwd<true> : tc32::tc32_pair_fwd<false>)
-        <<<static_cast<unsigned>(grid), tc32::kPairThreads, tc32::pair_smem_bytes(), stream>>>(a, maps);
-  } else if (kernel_id == RAYA_KERNEL_TC32_WS || kernel_id == RAYA_KERNEL_TC32_WS2 ||
-             (kernel_id == RAYA_KERNEL_TC32_STREAM && !stage_cycles)) {
+  } else if (kernel_id == RAYA_KERNEL_TC32_WS || kernel_id == RAYA_KERNEL_TC32_WS2) {
     if (d->head_dim != 64)
       return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tensor-core kernel needs head_dim 64, got %lld",
                   static_cast<long long>(d->head_dim));
@@ -499,11 +455,7 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     if (rows > 0x7fffffffull)
       return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %llu rows exceed the tensor-map row limit",
                   static_cast<unsigned long long>(rows));
-    if (kernel_id == RAYA_KERNEL_TC32_STREAM) {
-      const long long resident = std::min<long long>(grid, ctx->sms);  // one CTA per SM walks the row tiles
-      tc32::tc32_stream_fwd<<<static_cast<unsigned>(resident), tc32::kWsThreads, tc32::stream_smem_bytes(),
-                              stream>>>(a, maps);
-    } else {
+    {
       // UNITS row tiles per CTA: 1 (kernel 34), 4 where a slice is four row
       // tiles, else 2 (kernel 37); the stage-timing build where asked.
       const int units = kernel_id == RAYA_KERNEL_TC32_WS ? 1 : a.row_tiles == 4 ? 4 : 2;

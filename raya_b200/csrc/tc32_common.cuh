@@ -1,7 +1,8 @@
 // tc32_common.cuh — building blocks of the 3xTF32 tensor-core attention
 // kernels (sm_100a): tile sizes, tcgen05 instruction and shared-memory
 // descriptors, tensor-memory loads and stores, the TF32 operand split, the
-// TMA tile stores, and the shared-memory rings of the two-issuer kernel.
+// TMA tile stores, and the shared-memory rings of the two-issuer kernel
+// (tc32_ws.cuh).
 //
 // 3xTF32.  Every fp32 operand x (q, k, v and the softmax weights p) enters
 // the tensor core twice: as x itself, which kind::tf32 reads with its 13 low
@@ -42,13 +43,6 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
                                               uint64_t layout = kSwizzle128) {
   return static_cast<uint64_t>((addr >> 4) & 0x3FFF) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16) |
          (static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (layout << 61);
-}
-
-// Arrives once on `bar` when every MMA this thread has issued is complete.
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_addr(bar))
-               : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -98,30 +92,9 @@ __device__ __forceinline__ uint32_t chunk_offset(int r, int c4) {
 }
 
 // D (+)= A B with A read from tensor memory (M = 128 rows in lanes, K = 8
-// 32-bit columns) and B from a shared-memory descriptor.
-__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
-      : "memory");
-}
-
-// D (+)= A B with both operands from shared-memory descriptors.
-__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
-      : "memory");
-}
-
-// Elected-lane forms.  The whole issuing warp runs the issue loop (so its
-// operands are warp-uniform) and one lane, picked by elect.sync, issues.
+// 32-bit columns) and B from a shared-memory descriptor, in elected-lane
+// form: the whole issuing warp runs the issue loop (so its operands are
+// warp-uniform) and one lane, picked by elect.sync, issues.
 // Measured on B200 (M = 128, N = 64, K = 8, tf32): a chain of MMAs into one
 // accumulator issued this way runs at ~64 cycles per MMA, against ~120 when
 // a single lane issues from a divergent branch; two issuing warps with a
@@ -136,29 +109,14 @@ __device__ __forceinline__ void mma_tf32_ts_e(uint32_t d_tmem, uint32_t a_tmem, 
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
       : "memory");
 }
-__device__ __forceinline__ void mma_tf32_ss_e(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                              uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
-      "elect.sync r|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
-      : "memory");
-}
-// tcgen05.commit from the elected lane of a warp that runs the issue loop.
+// tcgen05.commit from the elected lane of a warp that runs the issue loop:
+// arrives once on `bar` when every MMA that lane issued is complete.
 __device__ __forceinline__ void mma_commit_e(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
       "elect.sync r|e, 0xffffffff;\n\t"
       "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_addr(bar))
       : "memory");
-}
-
-// K-major A (a 128-row q tile in two column halves of [128][32], 128-byte
-// swizzle): k-step s is column half s/4, byte 32*(s%4).
-__device__ __forceinline__ uint64_t q_desc(uint32_t base, int s) {
-  return smem_desc(base + (s >> 2) * (kBM * 128) + (s & 3) * 32, 16, 1024);
 }
 
 // K-major B (K hi/lo tile, 64 keys): k-step s is column half s/4, byte 32*(s%4).

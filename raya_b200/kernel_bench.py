@@ -73,7 +73,7 @@ def metadata(root: str, threads: int) -> dict:
         "label": LABELS.get(os.environ.get("RAYA_TARGET_MACHINE", ""), UNLABELED),
         "cpu_model": _cpu_model(), "logical_cpus": os.cpu_count() or 0,
         "physical_cpus": len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else 0,
-        "threads": threads, "features": ["tiled64", "ffma2", "tma"], "backend": "sm_100a",
+        "threads": threads, "features": ["tcgen05-3xtf32", "tiled64", "ffma2", "tma"], "backend": "sm_100a",
         "rustflags": "", "rustc": "", "git_commit": _git_commit(root),
         "timestamp": f"unix:{int(time.time())}",
         "gpu": props.name, "gpu_sms": props.multi_processor_count, "gpu_max_sm_clock": max_sm,
@@ -121,7 +121,7 @@ def run(root: str, cpu_rows=None) -> str:
             dvalid = torch.tensor([seq], dtype=torch.int32, device=dev)
             mean, sd = _time_calls(lambda: kern.attend_device(shape, params, q, k, v, out, valid_len=dvalid),
                                    SAMPLES)
-            st = rb.stage_times(shape, params, q, k, v, out, valid_len=dvalid)
+            st = rb.stage_times(shape, params, q, k, v, out, valid_len=dvalid, kernel=rb.KERNEL_AUTO)
             pairs, _ = rb.work(shape, params)
             results.append({
                 "kernel": "cuda-b200", "mask": name, "backend": "sm_100a", "seq": seq, "heads": HEADS,

@@ -205,9 +205,7 @@ def test_automatic_kernel_choice(mask, block, expect_tc):
     shape = _shape(heads=2, seq=1024, d=64)
     params = rb.AttnParams.new(mask, 1024, 64, block=block)
     kid = rb.kernel_for(shape, params)
-    if expect_tc == "stream":
-        assert kid == rb._lib.KERNEL_TC32_STREAM
-    elif expect_tc:
+    if expect_tc:
         assert kid == rb._lib.KERNEL_TC32_WS
     else:
         assert kid in _lib.KERNEL_TILED64_VARIANTS.values()

@@ -71,3 +71,15 @@ def test_noalloc_rejects_sequences_past_its_table(cuda_device):
     st = _lib.lib.raya_attn_forward_packed_noalloc(ctypes.byref(d), 16, 16, None, ctypes.c_float(10000.0), None)
     assert st == _lib.ERR_UNSUPPORTED
     assert "8192" in _lib.last_error()
+
+
+def test_noalloc_at_the_table_limit_and_without_rotation_past_it(cuda_device):
+    """seq exactly 8192 with the rotation (the whole built-in table in use),
+    and rope_theta 0 at a seq past 8192 (no table, no limit), each against
+    the workspace call."""
+    got, want = _both(batch=1, seq=8192, heads=1, theta=10000.0, seed=303)
+    assert np.isfinite(got).all()
+    assert_close(got, want, "seq 8192 with rotation")
+    got, want = _both(batch=1, seq=8192 + 300, heads=1, theta=0.0, seed=404)
+    assert np.isfinite(got).all()
+    assert_close(got, want, "seq 8492 without rotation")
