@@ -288,3 +288,22 @@ def test_automatic_choice_two_tile_form_for_many_long_block_tiles():
     one = _shape(heads=16, seq=8192, d=64, batch=1)  # 1024 tiles
     assert rb.kernel_for(one, params(128)) == rb.KERNEL_TC32_WS
     assert rb.kernel_for(c5, params(1024)) == rb.KERNEL_TC32_WS  # 3072 keys per span
+
+
+def test_rust_binding_matches_the_header():
+    """The FFI crate crates/raya-kernels-cuda (no cargo in this image, so it
+    is checked as text): every function its extern block declares is
+    exported by the library, and its #[repr(C)] descriptor has the fields of
+    raya_attn_desc in the header's order with the same widths."""
+    src = open(os.path.join(ROOT, "crates", "raya-kernels-cuda", "src", "lib.rs")).read()
+    block = src[src.index('extern "C" {'):]
+    block = block[:block.index("\n}\n")]
+    declared = set(re.findall(r"fn (raya_attn_\w+)\(", block))
+    assert declared and declared <= set(_lib.EXPORTS), declared - set(_lib.EXPORTS)
+    rust = re.findall(r"^\s+(\w+): (i64|i32|f32),$", src[src.index("struct RayaAttnDesc"):src.index("// raya_attn_status")],
+                      flags=re.M)
+    header = open(os.path.join(ROOT, "include", "raya_attn.h")).read()
+    body = header[header.index("typedef struct {"):header.index("} raya_attn_desc;")]
+    c = re.findall(r"(int64_t|int32_t|float) (\w+);", body)
+    width = {"i64": "int64_t", "i32": "int32_t", "f32": "float"}
+    assert [(n, width[t]) for n, t in rust] == [(n, t) for t, n in c]
