@@ -54,7 +54,8 @@ def parse():
     ap.add_argument("--no-gather", action="store_true", help="skip the timed output gather to rank 0 (N > 1)")
     ap.add_argument("--gather-reps", type=int, default=3)
     ap.add_argument("--halo", type=int, default=1)
-    ap.add_argument("--kernel", type=int, default=0, help="0 auto, 1 tiled64, 2 rowwise, 34 tc32_ws, 37 tc32_ws two-tile (3xTF32 tensor cores)")
+    ap.add_argument("--kernel", type=int, default=0, help="0 auto, 1 tiled64, 2 rowwise, 34 tc32_ws, 37 tc32_ws two-tile (3xTF32 tensor cores), "
+                    "40 tc16_ws, 41 tc16_ws two-tile (3xFP16 tensor cores)")
     ap.add_argument("--e2e-steps", type=int, default=3,
                     help="timed host-buffer calls (each copies the step's inputs in and its output out)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -263,6 +264,12 @@ def kernel_label(rb, chosen, shape, packed) -> str:
         return (("tc32_ws with four 128-row tiles (a whole slice) per CTA" if (shape.seq + 127) // 128 == 4
                  and not packed else "tc32_ws with two 128-row tiles per CTA")
                 + " (raya_b200/csrc/tc32_ws.cuh), kernel id 37")
+    if chosen == rb.KERNEL_TC16_WS:
+        return ("tc16_ws, 3xFP16 tcgen05 kind::f16 with power-of-two operand scaling, two MMA-issuing warps, "
+                "PV summed in fp32 registers (raya_b200/csrc/tc16_ws.cuh), kernel id 40")
+    if chosen == rb.KERNEL_TC16_WS2:
+        return ("tc16_ws persistent (one CTA per SM walking its 128-row tiles), 3xFP16 tcgen05 kind::f16 "
+                "(raya_b200/csrc/tc16_ws.cuh), kernel id 41")
     return f"tiled64 (raya_b200/csrc/tiled64.cuh), kernel id {chosen}"
 
 
@@ -330,7 +337,8 @@ def run_b200(args) -> None:
     chosen = (rb.kernel_for(shape, params, packed=args.packed, rope=args.rope_theta > 0)
               if args.kernel == rb.KERNEL_AUTO else args.kernel) if shape.batch > 0 else rb.KERNEL_AUTO
     tiled_ids = set(rb._lib.KERNEL_TILED64_VARIANTS.values()) | {rb.KERNEL_TILED64}
-    TENSOR_KERNELS = (rb.KERNEL_TC32_WS, rb.KERNEL_TC32_WS2)
+    F16_KERNELS = (rb.KERNEL_TC16_WS, rb.KERNEL_TC16_WS2)
+    TENSOR_KERNELS = (rb.KERNEL_TC32_WS, rb.KERNEL_TC32_WS2) + F16_KERNELS
     stream = torch.cuda.current_stream(dev)
 
     # Live FFMA peak of this GPU (the fp32-equivalent denominator: no FP32
@@ -443,14 +451,17 @@ def run_b200(args) -> None:
                "peak_source": f"MEASURED_PEAKS.json hbm_gbs (of {peak_kind})" if peak_kind == "measured"
                else "fallback copy bandwidth of this pool (of fallback)"}
     if chosen in TENSOR_KERNELS:
-        # 3xTF32 issues three TF32 products per fp32 product: the algorithmic
-        # tensor work is 3 x 4 * head_dim per allowed pair.  Dense TF32 runs at
-        # half the bf16 rate.
-        tf32_peak = peaks["bf16_tflops"] / 2
-        roofline = {"bound": "tensor", "achieved": round(3 * achieved_tf, 3), "peak": round(tf32_peak, 1),
-                    "unit": "TFLOP/s", "frac": round(3 * achieved_tf / tf32_peak, 4),
-                    "peak_source": f"dense TF32 = bf16_tflops / 2 (of {peak_kind})",
-                    "work": "3 TF32 products (hi*lo, lo*hi, hi*hi) x 4 * head_dim flops per allowed pair",
+        # Three tensor-core products per fp32 product (hi*lo, lo*hi, hi*hi):
+        # the algorithmic tensor work is 3 x 4 * head_dim per allowed pair.
+        # Dense fp16 runs at the bf16 rate, dense TF32 at half of it.
+        f16 = chosen in F16_KERNELS
+        t_peak = peaks["bf16_tflops"] if f16 else peaks["bf16_tflops"] / 2
+        roofline = {"bound": "tensor", "achieved": round(3 * achieved_tf, 3), "peak": round(t_peak, 1),
+                    "unit": "TFLOP/s", "frac": round(3 * achieved_tf / t_peak, 4),
+                    "peak_source": (f"dense fp16 = bf16_tflops (of {peak_kind})" if f16
+                                    else f"dense TF32 = bf16_tflops / 2 (of {peak_kind})"),
+                    "work": (f"3 {'fp16' if f16 else 'TF32'} products (hi*lo, lo*hi, hi*hi) x 4 * head_dim "
+                             "flops per allowed pair"),
                     "fp32_equivalent": {"achieved": round(achieved_tf, 3), "ffma_peak": round(ffma_tflops, 3),
                                         "frac": round(achieved_tf / ffma_tflops, 4)},
                     "traffic": traffic, "algorithmic_bytes": bytes_launch, "hbm": hbm_obj}

@@ -106,7 +106,18 @@ typedef enum {
    * the whole slice; head-major layout), one after the other, each run as a
    * CTA of its own (sharing only the CTA's launch, tensor-memory allocation
    * and valid_len loads). */
-  RAYA_KERNEL_TC32_WS2 = 37
+  RAYA_KERNEL_TC32_WS2 = 37,
+  /* The same pipeline on tcgen05 kind::f16 in 3xFP16: each fp32 operand is
+   * scaled by a power of two (per q row, per 64-key K or V tile) so that its
+   * largest element lies in [2^14, 2^15), then split into two fp16 parts;
+   * three products per tile at twice kind::tf32's rate per instruction.  The
+   * softmax removes the scales exactly.  head_dim 64, 128-row tiles, one
+   * per CTA. */
+  RAYA_KERNEL_TC16_WS = 40,
+  /* RAYA_KERNEL_TC16_WS as a persistent grid: one CTA per SM walks its
+   * 128-row tiles, every ring running on across them, so one tile's copies
+   * and products overlap the previous tile's tail. */
+  RAYA_KERNEL_TC16_WS2 = 41
 } raya_kernel_id;
 
 /* Argument checks of validate (attention.rs:128-170), extended to the batch

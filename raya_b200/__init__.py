@@ -22,7 +22,8 @@ _FROM_ATTENTION = (
     "sync_status", "validate", "work",
 )
 _FROM_LIB = (
-    "KERNEL_AUTO", "KERNEL_ROWWISE", "KERNEL_TC32_WS", "KERNEL_TC32_WS2", "KERNEL_TILED64",
+    "KERNEL_AUTO", "KERNEL_ROWWISE", "KERNEL_TC16_WS", "KERNEL_TC16_WS2", "KERNEL_TC32_WS", "KERNEL_TC32_WS2",
+    "KERNEL_TILED64",
     "LIB_PATH",
 )
 

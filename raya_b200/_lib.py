@@ -17,6 +17,8 @@ MASK_BLOCK, MASK_WINDOW, MASK_FULL = 0, 1, 2
 KERNEL_AUTO, KERNEL_TILED64, KERNEL_ROWWISE = 0, 1, 2
 KERNEL_TC32_WS = 34
 KERNEL_TC32_WS2 = 37
+KERNEL_TC16_WS = 40
+KERNEL_TC16_WS2 = 41
 KERNEL_TILED64_VARIANTS = {"w4r32": 16, "w4r16": 19, "w4r16p2": 20, "w4r32p2": 21}
 
 # Every symbol include/raya_attn.h declares (checked by the ABI test).

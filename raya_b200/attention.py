@@ -398,7 +398,7 @@ def stage_times(shape: AttnShape, params: AttnParams, q, k, v, out, valid_len=No
     per stage plus qk/softmax/pv percentages of their total
     (StageTimes::percentages, tiled/stages.rs:19-31).  ``kernel``: a tiled
     kernel (warp cycles per stage), or KERNEL_TC32_WS / KERNEL_TC32_WS2 /
-    KERNEL_AUTO for the tensor-core kernels (per-CTA cycles of QK^T and PV
+    KERNEL_TC16_WS / KERNEL_TC16_WS2 / KERNEL_AUTO for the tensor-core kernels (per-CTA cycles of QK^T and PV
     products in flight and of one softmax warp; these overlap in time)."""
     import torch
 

@@ -131,16 +131,35 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// is suspended by the hardware (until the phase completes, or for at most
+// about the hint) instead of spinning, so waiting warps leave the issue
+// slots of their sub-partition to the warps that have work.
+constexpr uint32_t kSuspendHintNs = 100000;  // 0.1 ms
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity), "n"(kSuspendHintNs)
+      : "memory");
+  return done != 0;
+}
+
 // Bounded wait on an mbarrier phase.  Gives up after `timeout_cycles`
 // (recording bit 0 in the device status word and raising the CTA's abort
 // flag so that its other warps stop waiting too).  Returns false on give-up.
+// Each try suspends for at most ~0.1 ms, so the bound and the abort flag are
+// checked at least that often.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag, int* status,
                                                   long long timeout_cycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_suspend(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > timeout_cycles) {
       *abort_flag = 1;

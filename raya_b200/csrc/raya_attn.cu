@@ -20,6 +20,7 @@
 #include "../../include/raya_attn.h"
 #include "common.cuh"
 #include "rowwise.cuh"
+#include "tc16_ws.cuh"
 #include "tc32_common.cuh"
 #include "tc32_ws.cuh"
 #include "tiled64.cuh"
@@ -224,6 +225,12 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
       e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(tc32::pipe_smem_bytes()));
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_ws smem)");
+    }
+    for (auto fn : {tc16::tc16_ws_fwd<tiled64::kHeadMajor, false>, tc16::tc16_ws_fwd<tiled64::kPacked, false>,
+                    tc16::tc16_ws_fwd<tiled64::kPacked, true>, tc16::tc16_ws_fwd<tiled64::kHeadMajor, false, true>}) {
+      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(tc16::smem_bytes()));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc16_ws smem)");
     }
     for (const PackedVariant& pv : kPacked) {
       for (auto fn : {pv.plain, pv.rope}) {
@@ -473,6 +480,31 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
       fn<<<static_cast<unsigned>((grid + units - 1) / units), tc32::kWsThreads, tc32::pipe_smem_bytes(), stream>>>(
           a, maps);
     }
+  } else if (kernel_id == RAYA_KERNEL_TC16_WS || kernel_id == RAYA_KERNEL_TC16_WS2) {
+    if (d->head_dim != 64)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: the tensor-core kernel needs head_dim 64, got %lld",
+                  static_cast<long long>(d->head_dim));
+    a.row_tiles = static_cast<int>((d->seq + tc16::kBM - 1) / tc16::kBM);
+    const long long grid = static_cast<long long>(d->batch) * d->heads * a.row_tiles;
+    if (grid > 0x7fffffffll)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
+    const uint64_t rows = static_cast<uint64_t>(d->batch) * d->heads * d->seq;
+    if (rows > 0x7fffffffull)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %llu rows exceed the tensor-map row limit",
+                  static_cast<unsigned long long>(rows));
+    tc32::PipeMaps maps;  // k, v and q all [64 rows][32] boxes under the 128-byte swizzle of 16-byte chunks
+    raya_attn_status st = encode_rows64(&maps.k, k, rows, tc16::kBN);
+    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.v, v, rows, tc16::kBN);
+    if (st == RAYA_ATTN_OK)
+      st = encode_slices3d(&maps.o, out, static_cast<uint64_t>(d->batch) * d->heads, static_cast<uint64_t>(d->seq));
+    if (st == RAYA_ATTN_OK) st = encode_rows64(&maps.q, q, rows, tc16::kBN);
+    if (st != RAYA_ATTN_OK) return st;
+    // kernel 40: one unit (128-row tile) per CTA; kernel 41: persistent, one
+    // CTA per SM walking its units.
+    const long long ctas = kernel_id == RAYA_KERNEL_TC16_WS ? grid : std::min<long long>(grid, ctx->sms);
+    auto fn = stage_cycles ? tc16::tc16_ws_fwd<tiled64::kHeadMajor, false, true>
+                           : tc16::tc16_ws_fwd<tiled64::kHeadMajor, false>;
+    fn<<<static_cast<unsigned>(std::max<long long>(ctas, 1)), tc16::kThreads, tc16::smem_bytes(), stream>>>(a, maps);
   } else if (stage_cycles) {
     return fail(RAYA_ATTN_ERR_UNSUPPORTED,
                 "unsupported: stage timing needs a tiled kernel or the two-issuer tensor-core kernel");
@@ -896,6 +928,25 @@ raya_attn_status launch_packed(DeviceCtx* ctx_dev, const raya_attn_desc* desc, c
     else
       (rope ? tc32::tc32_ws_fwd<tiled64::kPacked, true, 1> : tc32::tc32_ws_fwd<tiled64::kPacked, false, 1>)
           <<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), s>>>(a, maps);
+  } else if (pk == RAYA_KERNEL_TC16_WS || pk == RAYA_KERNEL_TC16_WS2) {
+    a.row_tiles = static_cast<int>((desc->seq + tc16::kBM - 1) / tc16::kBM);
+    const long long grid = static_cast<long long>(desc->batch) * desc->heads * a.row_tiles;
+    if (grid > 0x7fffffffll)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
+    if (rows > 0x7fffffffull)
+      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %llu rows exceed the tensor-map row limit",
+                  static_cast<unsigned long long>(rows));
+    tc32::PipeMaps maps;
+    st = encode_packed(&maps.q, qkv, rows, desc->heads, tc16::kBN);
+    if (st == RAYA_ATTN_OK)
+      st = encode_context(&maps.o, ctx, static_cast<uint64_t>(desc->batch), static_cast<uint64_t>(desc->seq),
+                          static_cast<uint64_t>(desc->heads));
+    if (st != RAYA_ATTN_OK) return st;
+    maps.k = maps.q;  // q, k and v: the same [64 rows][32] boxes of the packed tensor
+    maps.v = maps.q;
+    const long long ctas = pk == RAYA_KERNEL_TC16_WS ? grid : std::min<long long>(grid, ctx_dev->sms);
+    (rope ? tc16::tc16_ws_fwd<tiled64::kPacked, true> : tc16::tc16_ws_fwd<tiled64::kPacked, false>)
+        <<<static_cast<unsigned>(std::max<long long>(ctas, 1)), tc16::kThreads, tc16::smem_bytes(), s>>>(a, maps);
   } else {
     const int id = tuned_tiled(desc);
     const PackedVariant* pv = nullptr;

@@ -35,7 +35,8 @@ LONG_SPANS = [
 ]
 
 
-@pytest.mark.parametrize("kernel", [rb.KERNEL_AUTO, rb.KERNEL_TC32_WS, rb.KERNEL_TC32_WS2, rb.KERNEL_TILED64])
+@pytest.mark.parametrize("kernel", [rb.KERNEL_AUTO, rb.KERNEL_TC32_WS, rb.KERNEL_TC32_WS2, rb.KERNEL_TC16_WS,
+                                    rb.KERNEL_TC16_WS2, rb.KERNEL_TILED64])
 @pytest.mark.parametrize("name,p", LONG_SPANS, ids=[n for n, _ in LONG_SPANS])
 def test_values_with_nonzero_mean_over_long_spans(cuda_device, kernel, name, p):
     q, k, v = oracle.qkv(p.numel, 2024)

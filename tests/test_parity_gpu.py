@@ -18,11 +18,13 @@ from _util import (assert_close, cuda_device_run, cuda_host_run, load_golden,
 
 pytestmark = pytest.mark.gpu
 
-KERNELS_D64 = [rb.KERNEL_TILED64, rb.KERNEL_ROWWISE, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_WS2]
+KERNELS_D64 = [rb.KERNEL_TILED64, rb.KERNEL_ROWWISE, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_WS2,
+               rb._lib.KERNEL_TC16_WS, rb._lib.KERNEL_TC16_WS2]
 # every compiled variant of the tiled kernel (warps per CTA x K/V stages)
 TILED_VARIANTS = [rb.KERNEL_TILED64] + sorted(rb._lib.KERNEL_TILED64_VARIANTS.values())
 # every head_dim-64 kernel: the FFMA variants, rowwise, and the 3xTF32 tensor-core kernels
-ALL_D64 = TILED_VARIANTS + [rb.KERNEL_ROWWISE, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_WS2]
+ALL_D64 = TILED_VARIANTS + [rb.KERNEL_ROWWISE, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_WS2,
+                            rb._lib.KERNEL_TC16_WS, rb._lib.KERNEL_TC16_WS2]
 B3 = dict(mask=oracle.MASK_BLOCK, block=128, halo=1)
 W64 = dict(mask=oracle.MASK_WINDOW, window=64)
 
@@ -96,8 +98,8 @@ def test_masks_are_exact(cuda_device, mask, d):
     p = oracle.Problem(1, 1, n, d, **mask)
     q, k = oracle.rand_vec(p.numel, 5), oracle.rand_vec(p.numel, 6)
     m = rb.Mask.BLOCK3 if mask is B3 else rb.Mask.WINDOW64
-    kernels = [rb.KERNEL_AUTO] + ([rb.KERNEL_ROWWISE, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_WS2]
-                                  if d == 64 else [])
+    kernels = [rb.KERNEL_AUTO] + ([rb.KERNEL_ROWWISE, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC32_WS2,
+                                   rb._lib.KERNEL_TC16_WS, rb._lib.KERNEL_TC16_WS2] if d == 64 else [])
     for kernel in kernels:
         for j in [0, 1, 63, 64, 65, 127, 128, 129, 191, 255, 256, 299]:
             v = np.zeros(p.numel, dtype=np.float32)
@@ -262,13 +264,14 @@ def test_host_call_copies_only_valid_rows(cuda_device, mask, valid):
 
 
 @pytest.mark.parametrize("mask", [B3, W64, dict(mask=oracle.MASK_FULL)], ids=["block3", "window64", "full"])
-@pytest.mark.parametrize("kernel", [rb._lib.KERNEL_TC32_WS2, rb._lib.KERNEL_TC32_WS, rb.KERNEL_AUTO])
+@pytest.mark.parametrize("kernel", [rb._lib.KERNEL_TC32_WS2, rb._lib.KERNEL_TC32_WS, rb._lib.KERNEL_TC16_WS2,
+                                    rb._lib.KERNEL_TC16_WS, rb.KERNEL_AUTO])
 @pytest.mark.parametrize("seq", [700, 512], ids=["seq700", "seq512"])
 def test_many_units_per_sm(cuda_device, mask, kernel, seq):
     """More (slice, 128-row) units than SMs, so several CTAs run on each SM
     in turn, with padding-only units (valid 0 and short sequences) and ragged
-    tails.  At seq 512 a slice is four row tiles (kernel 37 then runs four
-    per CTA)."""
+    tails.  At seq 512 a slice is four row tiles (kernels 37 and 41 then run
+    four per CTA)."""
     rng = np.random.default_rng(123)
     batch = 48 if mask is not W64 else 40
     p = oracle.Problem(batch, 4, seq, 64, **mask)

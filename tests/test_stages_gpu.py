@@ -34,7 +34,8 @@ def _key_tiles(p, valid, bm=128, bn=64):
     return total * p.heads
 
 
-@pytest.mark.parametrize("kernel", [rb.KERNEL_TILED64, rb.KERNEL_TC32_WS, rb.KERNEL_TC32_WS2, rb.KERNEL_AUTO])
+@pytest.mark.parametrize("kernel", [rb.KERNEL_TILED64, rb.KERNEL_TC32_WS, rb.KERNEL_TC32_WS2, rb.KERNEL_TC16_WS,
+                                    rb.KERNEL_TC16_WS2, rb.KERNEL_AUTO])
 @pytest.mark.parametrize("block,seq", [(64, 1024), (128, 2048), (64, 512)], ids=["b64", "b128", "b64-seq512"])
 def test_stage_timing(cuda_device, kernel, block, seq):
     import torch
@@ -55,5 +56,5 @@ def test_stage_timing(cuda_device, kernel, block, seq):
         assert st[name] > 0, (name, st)
     assert abs(st["qk_pct"] + st["softmax_pct"] + st["pv_pct"] - 100.0) < 1e-6
     chosen = rb.kernel_for(shape, params) if kernel == rb.KERNEL_AUTO else kernel
-    if chosen in (rb.KERNEL_TC32_WS, rb.KERNEL_TC32_WS2):
+    if chosen in (rb.KERNEL_TC32_WS, rb.KERNEL_TC32_WS2, rb.KERNEL_TC16_WS, rb.KERNEL_TC16_WS2):
         assert st["tiles"] == _key_tiles(p, valid), st
