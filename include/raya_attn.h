@@ -112,7 +112,8 @@ typedef enum {
    * largest element lies in [2^14, 2^15), then split into two fp16 parts;
    * three products per tile at twice kind::tf32's rate per instruction.  The
    * softmax removes the scales exactly.  head_dim 64, 128-row tiles, one
-   * per CTA. */
+   * per CTA; raya_attn_forward_ex only (the packed entry points use the TF32
+   * kernels). */
   RAYA_KERNEL_TC16_WS = 40,
   /* RAYA_KERNEL_TC16_WS as a persistent grid: one CTA per SM walks its
    * 128-row tiles, every ring running on across them, so one tile's copies

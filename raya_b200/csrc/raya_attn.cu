@@ -226,8 +226,7 @@ raya_attn_status ensure_ready(int dev, DeviceCtx** out) {
                                static_cast<int>(tc32::pipe_smem_bytes()));
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc32_ws smem)");
     }
-    for (auto fn : {tc16::tc16_ws_fwd<tiled64::kHeadMajor, false>, tc16::tc16_ws_fwd<tiled64::kPacked, false>,
-                    tc16::tc16_ws_fwd<tiled64::kPacked, true>, tc16::tc16_ws_fwd<tiled64::kHeadMajor, false, true>}) {
+    for (auto fn : {tc16::tc16_ws_fwd<tiled64::kHeadMajor>, tc16::tc16_ws_fwd<tiled64::kHeadMajor, true>}) {
       e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(tc16::smem_bytes()));
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc16_ws smem)");
@@ -502,8 +501,8 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
     // kernel 40: one unit (128-row tile) per CTA; kernel 41: persistent, one
     // CTA per SM walking its units.
     const long long ctas = kernel_id == RAYA_KERNEL_TC16_WS ? grid : std::min<long long>(grid, ctx->sms);
-    auto fn = stage_cycles ? tc16::tc16_ws_fwd<tiled64::kHeadMajor, false, true>
-                           : tc16::tc16_ws_fwd<tiled64::kHeadMajor, false>;
+    auto fn = stage_cycles ? tc16::tc16_ws_fwd<tiled64::kHeadMajor, true>
+                           : tc16::tc16_ws_fwd<tiled64::kHeadMajor>;
     fn<<<static_cast<unsigned>(std::max<long long>(ctas, 1)), tc16::kThreads, tc16::smem_bytes(), stream>>>(a, maps);
   } else if (stage_cycles) {
     return fail(RAYA_ATTN_ERR_UNSUPPORTED,
@@ -928,25 +927,6 @@ raya_attn_status launch_packed(DeviceCtx* ctx_dev, const raya_attn_desc* desc, c
     else
       (rope ? tc32::tc32_ws_fwd<tiled64::kPacked, true, 1> : tc32::tc32_ws_fwd<tiled64::kPacked, false, 1>)
           <<<static_cast<unsigned>(grid), tc32::kWsThreads, tc32::pipe_smem_bytes(), s>>>(a, maps);
-  } else if (pk == RAYA_KERNEL_TC16_WS || pk == RAYA_KERNEL_TC16_WS2) {
-    a.row_tiles = static_cast<int>((desc->seq + tc16::kBM - 1) / tc16::kBM);
-    const long long grid = static_cast<long long>(desc->batch) * desc->heads * a.row_tiles;
-    if (grid > 0x7fffffffll)
-      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %lld CTAs exceed the grid limit", grid);
-    if (rows > 0x7fffffffull)
-      return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %llu rows exceed the tensor-map row limit",
-                  static_cast<unsigned long long>(rows));
-    tc32::PipeMaps maps;
-    st = encode_packed(&maps.q, qkv, rows, desc->heads, tc16::kBN);
-    if (st == RAYA_ATTN_OK)
-      st = encode_context(&maps.o, ctx, static_cast<uint64_t>(desc->batch), static_cast<uint64_t>(desc->seq),
-                          static_cast<uint64_t>(desc->heads));
-    if (st != RAYA_ATTN_OK) return st;
-    maps.k = maps.q;  // q, k and v: the same [64 rows][32] boxes of the packed tensor
-    maps.v = maps.q;
-    const long long ctas = pk == RAYA_KERNEL_TC16_WS ? grid : std::min<long long>(grid, ctx_dev->sms);
-    (rope ? tc16::tc16_ws_fwd<tiled64::kPacked, true> : tc16::tc16_ws_fwd<tiled64::kPacked, false>)
-        <<<static_cast<unsigned>(std::max<long long>(ctas, 1)), tc16::kThreads, tc16::smem_bytes(), s>>>(a, maps);
   } else {
     const int id = tuned_tiled(desc);
     const PackedVariant* pv = nullptr;

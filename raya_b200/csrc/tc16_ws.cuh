@@ -157,11 +157,33 @@ __device__ __forceinline__ uint32_t pack_f16x2(float e0, float e1) {
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(e1), "f"(e0));
   return r;
 }
-// Elements (e0, e1) -> packed hi and lo words.
+// Elements (e0, e1) -> packed hi and lo words (lo = e - hi, one packed FMA).
 __device__ __forceinline__ void split2(float e0, float e1, uint32_t& h, uint32_t& l) {
   const float h0 = hi_part(e0), h1 = hi_part(e1);
   h = pack_f16x2(h0, h1);
-  l = pack_f16x2(__fsub_rn(e0, h0), __fsub_rn(e1, h1));
+  const float2 lo = __ffma2_rn(make_float2(h0, h1), make_float2(-1.f, -1.f), make_float2(e0, e1));
+  l = pack_f16x2(lo.x, lo.y);
+}
+// max of three floats in one instruction.
+__device__ __forceinline__ float fmax3(float x, float y, float z) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(x), "f"(y), "f"(z));
+  return r;
+}
+// 16 consecutive fp32 columns of this thread's TMEM lane (load and wait in
+// one statement).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // D (+)= A B, kind::f16, A from tensor memory, in elected-lane form (the
@@ -191,6 +213,13 @@ __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t* v) {
       "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
 }
+// 8 packed 32-bit columns of this thread's lane; completion is awaited by
+// tmem_wait_st.
+__device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
 // One 16-byte shared-memory store of four 32-bit words.
 __device__ __forceinline__ void sts128u(uint32_t addr, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
@@ -206,15 +235,6 @@ __device__ __forceinline__ void load_box(void* dst, const CUtensorMap* map, int 
     tiled64::tma_load_2d(dst, map, x, y, bar);
   else
     tiled64::tma_load_4d(dst, map, x, head, which, y, bar);
-}
-
-// raya's rotary embedding (ops.rs:110-141, rotate-half form) of one element
-// pair, unfused f32 as the reference computes it.
-__device__ __forceinline__ void rot(float& x, float& y, float c, float sn) {
-  const float nx = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
-  const float ny = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
-  x = nx;
-  y = ny;
 }
 
 // One unit (a 128-row tile of one (batch, head) slice): its rows, keys and
@@ -265,25 +285,21 @@ __device__ __forceinline__ Unit unit_info(const AttnArgs& a, unsigned unit) {
 }
 
 
-// LAYOUT: tiled64::kHeadMajor (q, k, v, out as [batch*heads*seq][64]) or
-// tiled64::kPacked (q, k, v read in place from the packed projection
-// [batch*seq][3][heads][64], the output written as the context
-// [batch*seq][heads][64]: encoder.rs:34-92).  ROPE: q and k rotated first
-// (packed layout only): q rows by the softmax threads, K tiles by the K split
-// group.  TIMED: the stage-timing build (the counterpart of the reference's
-// StageTimes, tiled/stages.rs:1-31): clock64 cycles per CTA added into
-// a.stage_cycles — [kStageQk] QK^T products in flight (issue to completion:
-// in this build the QK issuer waits for each QK's completion), [kStageSoftmax]
-// one softmax warp's work per tile (S read to P stored), [kStagePv] PV
-// products in flight (likewise), [kStageKWait] the QK issuer waiting for K's
-// split, [kStageVWait] the PV issuer waiting for P and V's split,
-// [kStageRefill] one K split thread's work, [kStageTiles] key tiles,
-// [kStageTotal] thread 0's cycles over the CTA's units.  The stages overlap
-// in time; read them as proportions.
-template <int LAYOUT, bool ROPE, bool TIMED = false>
+// LAYOUT: tiled64::kHeadMajor (q, k, v, out as [batch*heads*seq][64]); the
+// caller's packed layout runs on tc32_ws.cuh.  TIMED: the stage-timing build
+// (the counterpart of the reference's StageTimes, tiled/stages.rs:1-31):
+// clock64 cycles per CTA added into a.stage_cycles — [kStageQk] QK^T products
+// in flight (issue to completion: in this build the QK issuer waits for each
+// QK's completion), [kStageSoftmax] one softmax warp's work per tile (S read
+// to P stored), [kStagePv] PV products in flight (likewise), [kStageKWait]
+// the QK issuer waiting for K's split, [kStageVWait] the PV issuer waiting
+// for P and V's split, [kStageRefill] one K split thread's work,
+// [kStageTiles] key tiles, [kStageTotal] thread 0's cycles over the CTA's
+// units.  The stages overlap in time; read them as proportions.
+template <int LAYOUT, bool TIMED = false>
 __global__ void __launch_bounds__(kThreads, 1)
     tc16_ws_fwd(const __grid_constant__ AttnArgs a, const __grid_constant__ tc32::PipeMaps maps) {
-  static_assert(!ROPE || LAYOUT == tiled64::kPacked, "the rotation is fused into the packed layout only");
+  static_assert(LAYOUT == tiled64::kHeadMajor, "the packed layout runs on tc32_ws.cuh");
   using namespace tc32;  // tensor-memory, barrier and TMA-store helpers
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
@@ -402,58 +418,63 @@ __global__ void __launch_bounds__(kThreads, 1)
       return nunits;
     };
     // The q row of unit u (the CTA's uidx-th) scaled by 2^eq and split into
-    // Q buffer uidx % 2; qmul = qscale * 2^-eq.  False after a timeout.
+    // Q buffer uidx % 2; qmul = qscale * 2^-eq.  False after a timeout.  It
+    // runs inside the previous unit's tile loop, next to that unit's O row,
+    // so it holds 32 elements at a time: pass 1 takes the row's largest
+    // magnitude, pass 2 reloads, scales, splits and stores.  Piece p is
+    // elements 16p..16p+15 and 16p+32..16p+47.
     auto prepare_q = [&](const Unit& u, uint32_t uidx, float& qmul) {
       const int qb = static_cast<int>(uidx & 1u);
       const int row = u.r0 + tid;
-      float4 qcs[ROPE ? 16 : 1];
-      if constexpr (ROPE) {
-        const float4* t = reinterpret_cast<const float4*>(a.rope_cs + static_cast<size_t>(min(row, seq - 1)) * 64);
-#pragma unroll
-        for (int i4 = 0; i4 < 16; ++i4) qcs[i4] = __ldg(t + i4);
-      }
       const bool wq = wait(&sm.q_full, uidx & 1u);
-      float qf[64];
+      const bool live = wq && row < u.valid;
       const uint32_t qs = smem_addr(&sm.q[0][0][0]);
+      auto piece = [&](int p, float* x, float* y) {  // x: elements 16p.., y: 16p+32..
 #pragma unroll
-      for (int c4 = 0; c4 < 16; ++c4) {
-        const float4 x =
-            (wq && row < u.valid) ? lds128(qs + chunk_offset<kBM>(tid, c4)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        qf[4 * c4] = x.x;
-        qf[4 * c4 + 1] = x.y;
-        qf[4 * c4 + 2] = x.z;
-        qf[4 * c4 + 3] = x.w;
-      }
-      mbar_arrive(&sm.q_empty);  // the producer may load the next unit's q
-      if constexpr (ROPE) {
-        if (wq && row < u.valid) {
-#pragma unroll
-          for (int i4 = 0; i4 < 16; ++i4) {
-            rot(qf[2 * i4], qf[2 * i4 + 32], qcs[i4].x, qcs[i4].y);
-            rot(qf[2 * i4 + 1], qf[2 * i4 + 33], qcs[i4].z, qcs[i4].w);
-          }
+        for (int c = 0; c < 4; ++c) {
+          const float4 v0 = live ? lds128(qs + chunk_offset<kBM>(tid, 4 * p + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 v1 = live ? lds128(qs + chunk_offset<kBM>(tid, 8 + 4 * p + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          x[4 * c] = v0.x; x[4 * c + 1] = v0.y; x[4 * c + 2] = v0.z; x[4 * c + 3] = v0.w;
+          y[4 * c] = v1.x; y[4 * c + 1] = v1.y; y[4 * c + 2] = v1.z; y[4 * c + 3] = v1.w;
         }
-      }
+      };
       float fm = 0.f;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) fm = fmaxf(fm, fabsf(qf[i]));
+      for (int p = 0; p < 2; ++p) {
+        float x[16], y[16];
+        piece(p, x, y);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) fm = fmaxf(fm, fmaxf(fabsf(x[k]), fabsf(y[k])));
+      }
       const int eq = scale_exp(__float_as_uint(fm));
       const float sq = pow2(eq);
       qmul = a.qscale * pow2(-eq);
       // Q buffer qb is free once the QK products of unit uidx-2 are complete.
       bool wt = wq;
       if (uidx >= 2 && wt) wt = wait(&sm.q_tfree[qb], ((uidx - 2) >> 1) & 1u);
-      if (__any_sync(0xffffffffu, !wt)) return false;
-      tc_fence_after();
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t h[16], l[16];
-#pragma unroll
-        for (int c = 0; c < 16; ++c)
-          split2(qf[32 * half + 2 * c] * sq, qf[32 * half + 2 * c + 1] * sq, h[c], l[c]);
-        tmem_st16u(tmem + lane_off + col_qh(qb) + 16 * half, h);
-        tmem_st16u(tmem + lane_off + col_qh(qb) + 32 + 16 * half, l);
+      if (__any_sync(0xffffffffu, !wt)) {
+        mbar_arrive(&sm.q_empty);
+        return false;
       }
+      tc_fence_after();
+      const uint32_t qh = tmem + lane_off + col_qh(qb);
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        float x[16], y[16];
+        piece(p, x, y);
+        uint32_t hx[8], lx[8], hy[8], ly[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          split2(x[2 * k] * sq, x[2 * k + 1] * sq, hx[k], lx[k]);
+          split2(y[2 * k] * sq, y[2 * k + 1] * sq, hy[k], ly[k]);
+        }
+        // column c holds elements 2c, 2c+1: x -> columns 8p..8p+7, y -> 16+8p..
+        tmem_st8u(qh + 8 * p, hx);
+        tmem_st8u(qh + 16 + 8 * p, hy);
+        tmem_st8u(qh + 32 + 8 * p, lx);
+        tmem_st8u(qh + 48 + 8 * p, ly);
+      }
+      mbar_arrive(&sm.q_empty);  // the producer may load the next unit's q
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&sm.q_ready[qb]);
@@ -493,51 +514,67 @@ __global__ void __launch_bounds__(kThreads, 1)
         // 2^-ek of this K tile; never below the smallest normal float, so that
         // a masked -inf times it stays -inf (only reached for q rows ~2^-100)
         const float mult = fmaxf(qmul * sm.kfac[g % kMeta], 1.17549435e-38f);
-        float sv[64];
-        tmem_ld32(tmem + lane_off + col_s(pb), sv);
-        tmem_ld32(tmem + lane_off + col_s(pb) + 32, sv + 32);
-        tc_fence_before();
-        mbar_arrive(&sm.s_free[pb]);  // QK(g+2) may overwrite this S buffer
-
-        if (!(rlo <= kt && rhi >= kt + kBN)) {
+        const bool full = rlo <= kt && rhi >= kt + kBN;
+        const uint32_t sa = tmem + lane_off + col_s(pb);
+        float mraw;
+        {  // pass 1 over S(g): the row max (masked keys -inf)
+          float sv[64];
+          tmem_ld32(sa, sv);
+          tmem_ld32(sa + 32, sv + 32);
+          if (!full) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (static_cast<unsigned>(kt + c - rlo) >= static_cast<unsigned>(rhi - rlo)) sv[c] = -INFINITY;
+            for (int c = 0; c < 64; ++c)
+              if (static_cast<unsigned>(kt + c - rlo) >= static_cast<unsigned>(rhi - rlo)) sv[c] = -INFINITY;
+          }
+          float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+          for (int c = 4; c < 64; c += 8)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) m4[q] = fmax3(m4[q], sv[c + q], sv[c + 4 + q]);
+          mraw = fmax3(fmaxf(m4[0], m4[1]), m4[2], m4[3]);
         }
-        float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
-#pragma unroll
-        for (int c = 4; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], sv[c]);
-        const float mc = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * mult;
+        const float mc = mraw * mult;
         float alpha = 1.f;
         if (mc > m_used + kRescaleLog2) {
           alpha = ex2(m_used - mc);
           m_used = mc;
         }
         const float mbase = m_used == -INFINITY ? 0.f : m_used;
-        float rs = 0.f;
-#pragma unroll
-        for (int c = 0; c < 64; c += 4) {
-          sv[c] = ex2(fmaf(sv[c], mult, -mbase));
-          sv[c + 1] = ex2(fmaf(sv[c + 1], mult, -mbase));
-          sv[c + 2] = ex2(fmaf(sv[c + 2], mult, -mbase));
-          sv[c + 3] = ex2(fmaf(sv[c + 3], mult, -mbase));
-          rs += (sv[c] + sv[c + 1]) + (sv[c + 2] + sv[c + 3]);
-        }
-        lsum = fmaf(lsum, alpha, rs);
 
         if (g >= 2) {  // P buffer pb is free once PV(g-2) is complete
           w = wait(&sm.pv_done2[pb], static_cast<uint32_t>((g - 2) >> 1) & 1u);
           if (__any_sync(0xffffffffu, !w)) { ok = false; break; }
           tc_fence_after();
         }
-        {
-          uint32_t h[32], l[32];
+        // pass 2, 16 columns at a time (a rolled loop: the code stays small
+        // for the instruction cache): p = 2^(s * mult - mbase), the row sum,
+        // and p's hi and lo parts into P buffer pb.
+        float2 rs2 = make_float2(0.f, 0.f);
+        const uint32_t ph = tmem + lane_off + col_ph(pb);
+        const float2 mult2 = make_float2(mult, mult), nb2 = make_float2(-mbase, -mbase);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float s16[16];
+          tmem_ld16(sa + 16 * c, s16);
+          if (!full) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) split2(sv[2 * c], sv[2 * c + 1], h[c], l[c]);
-          const uint32_t ph = tmem + lane_off + col_ph(pb);
-          tmem_st32u(ph, h);
-          tmem_st32u(ph + 32, l);
+            for (int i = 0; i < 16; ++i)
+              if (static_cast<unsigned>(kt + 16 * c + i - rlo) >= static_cast<unsigned>(rhi - rlo)) s16[i] = -INFINITY;
+          }
+          uint32_t h[8], l[8];
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const float2 arg = __ffma2_rn(make_float2(s16[i], s16[i + 1]), mult2, nb2);
+            const float p0 = ex2(arg.x), p1 = ex2(arg.y);
+            rs2 = __fadd2_rn(rs2, make_float2(p0, p1));
+            split2(p0, p1, h[i >> 1], l[i >> 1]);
+          }
+          tmem_st8u(ph + 8 * c, h);
+          tmem_st8u(ph + 32 + 8 * c, l);
         }
+        tc_fence_before();
+        mbar_arrive(&sm.s_free[pb]);  // QK(g+2) may overwrite this S buffer
+        lsum = fmaf(lsum, alpha, rs2.x + rs2.y);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&sm.p_ready2[pb]);  // PV(g) may start
@@ -556,12 +593,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tmem + lane_off + col_o(gp & 1) + 32, tt + 32);
           tc_fence_before();
           mbar_arrive(&sm.o_free[gp & 1]);  // PV(g+1) may overwrite this partial
+          const float2 vf2 = make_float2(vf, vf), al2 = make_float2(alpha, alpha);
           if (rescale) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) o[i] = __fmul_rn(fmaf(tt[i], vf, o[i]), alpha);
+            for (int i = 0; i < 64; i += 2) {
+              const float2 r =
+                  __fmul2_rn(__ffma2_rn(make_float2(tt[i], tt[i + 1]), vf2, make_float2(o[i], o[i + 1])), al2);
+              o[i] = r.x;
+              o[i + 1] = r.y;
+            }
           } else {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) o[i] = fmaf(tt[i], vf, o[i]);
+            for (int i = 0; i < 64; i += 2) {
+              const float2 r = __ffma2_rn(make_float2(tt[i], tt[i + 1]), vf2, make_float2(o[i], o[i + 1]));
+              o[i] = r.x;
+              o[i + 1] = r.y;
+            }
           }
         }
         if constexpr (TIMED) c_a += static_cast<unsigned long long>(clock64() - c_s0);
@@ -583,8 +630,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem + lane_off + col_o(gp & 1) + 32, tt + 32);
         tc_fence_before();
         mbar_arrive(&sm.o_free[gp & 1]);
+        const float2 vf2 = make_float2(vf, vf);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) o[i] = fmaf(tt[i], vf, o[i]);
+        for (int i = 0; i < 64; i += 2) {
+          const float2 r = __ffma2_rn(make_float2(tt[i], tt[i + 1]), vf2, make_float2(o[i], o[i + 1]));
+          o[i] = r.x;
+          o[i + 1] = r.y;
+        }
       }
       // This row, normalised (+0.0f past valid_len), straight to global memory.
       if (row < seq) {
@@ -610,23 +662,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp < 12) {
-    // ---------------- split groups: K (warps 4-7), V (warps 8-11) ----------------
+    // ---------------- split groups: K (warps 4-7), V (warps 8-11), one code path ----------------
     const bool is_v = warp >= 8;
     const int gt = tid - (is_v ? 256 : 128), gw = gt >> 5, lane = tid & 31;
     const int gbar = is_v ? kVBarrier : kKBarrier;
-    // K: two pair-units per thread, (row r, chunk c < 4) with its partner
-    // chunk c + 4 (elements 8c..8c+7 and 8c+32..8c+39, which the rotation
-    // pairs up): r = gt / 4 + 32 i, c = gt % 4.  V: four units, (row r,
-    // chunk c): r = gt / 8 + 16 i, c = gt % 8.  Either way 32 elements, and
-    // the offsets of unit i are those of unit 0 plus i times a fixed stride
-    // (the swizzle depends on r % 8 only).
-    const int r0k = gt >> 2, ck = gt & 3, r0v = gt >> 3, cv = gt & 7;
+    // Four units per thread, (row r, chunk c) = elements 8c..8c+7 of row r:
+    // r = gt / 8 + 16 i, c = gt % 8; the offsets of unit i are those of unit
+    // 0 plus 16 rows (the swizzle depends on r % 8 only).
+    const int r0s = gt >> 3, cs = gt & 7;
     // raw tile: 16-byte chunk c4 of row r at chunk_offset<kBN>(r, c4)
     // (swizzled: chunks 2c and 2c + 1 need not be adjacent)
-    const uint32_t koff_a0 = chunk_offset<kBN>(r0k, 2 * ck), koff_a1 = chunk_offset<kBN>(r0k, 2 * ck + 1);
-    const uint32_t koff_b0 = chunk_offset<kBN>(r0k, 8 + 2 * ck), koff_b1 = chunk_offset<kBN>(r0k, 9 + 2 * ck);
-    const uint32_t voff0 = chunk_offset<kBN>(r0v, 2 * cv), voff1 = chunk_offset<kBN>(r0v, 2 * cv + 1);
-    const uint32_t kop_a = op_off(r0k, ck), kop_b = op_off(r0k, ck + 4), vop = op_off(r0v, cv);
+    const uint32_t off0 = chunk_offset<kBN>(r0s, 2 * cs), off1 = chunk_offset<kBN>(r0s, 2 * cs + 1);
+    const uint32_t oop = op_off(r0s, cs);
+    uint64_t* const ready = is_v ? sm.v_ready : sm.k_ready;
+    uint64_t* const freed = is_v ? sm.v_free : sm.k_free;
+    uint64_t* const meta = is_v ? sm.vmeta : sm.kmeta;
+    float* const fac = is_v ? sm.vfac : sm.kfac;
+    const int op_h = is_v ? kOpVh : kOpKh;
     unsigned long long c_a = 0;
     int g = 0;
     bool ok = true;
@@ -640,124 +692,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (TIMED) c_k0 = clock64();
         const int kt = (u.t_begin + t) * kBN;
         const int nv = min(kBN, u.valid - kt);  // valid rows of this tile (>= 1)
-        // With the rotation: (cos, sin) of this thread's K pairs, loaded
-        // while the tile is in flight.
-        float4 kcs[ROPE ? 2 : 1][ROPE ? 4 : 1];
-        if constexpr (ROPE) {
-          if (!is_v) {
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              const int pos = kt + r0k + 32 * i;
-              if (pos < seq) {
-                const float4* tp =
-                    reinterpret_cast<const float4*>(a.rope_cs + static_cast<size_t>(pos) * 64 + 16 * ck);
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) kcs[i][q4] = __ldg(tp + q4);
-              }
-            }
-          }
-        }
         float x[32];
         uint32_t mx = 0;
         bool w = wait(&sm.raw_full[s], static_cast<uint32_t>(g / kRawStages) & 1u);
         if (w) {
           const uint32_t base = smem_addr(&sm.raw[s][is_v ? 1 : 0][0][0][0]);
-          if (!is_v) {
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              if (r0k + 32 * i < nv) {
-                const uint32_t o = static_cast<uint32_t>(i * 32 * 128);
-                const float4 x0 = lds128(base + koff_a0 + o), x1 = lds128(base + koff_a1 + o);
-                const float4 y0 = lds128(base + koff_b0 + o), y1 = lds128(base + koff_b1 + o);
-                float* e = x + 16 * i;
-                e[0] = x0.x; e[1] = x0.y; e[2] = x0.z; e[3] = x0.w; e[4] = x1.x; e[5] = x1.y; e[6] = x1.z;
-                e[7] = x1.w; e[8] = y0.x; e[9] = y0.y; e[10] = y0.z; e[11] = y0.w; e[12] = y1.x; e[13] = y1.y;
-                e[14] = y1.z; e[15] = y1.w;
-              } else {  // keys at or past valid_len: exact zeros
+          for (int i = 0; i < 4; ++i) {
+            if (r0s + 16 * i < nv) {
+              const uint32_t o = static_cast<uint32_t>(i * 16 * 128);
+              const float4 x0 = lds128(base + off0 + o), x1 = lds128(base + off1 + o);
+              float* e = x + 8 * i;
+              e[0] = x0.x; e[1] = x0.y; e[2] = x0.z; e[3] = x0.w; e[4] = x1.x; e[5] = x1.y; e[6] = x1.z;
+              e[7] = x1.w;
+            } else {  // keys at or past valid_len: exact zeros
 #pragma unroll
-                for (int q = 0; q < 16; ++q) x[16 * i + q] = 0.f;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              if (r0v + 16 * i < nv) {
-                const uint32_t o = static_cast<uint32_t>(i * 16 * 128);
-                const float4 x0 = lds128(base + voff0 + o), x1 = lds128(base + voff1 + o);
-                float* e = x + 8 * i;
-                e[0] = x0.x; e[1] = x0.y; e[2] = x0.z; e[3] = x0.w; e[4] = x1.x; e[5] = x1.y; e[6] = x1.z;
-                e[7] = x1.w;
-              } else {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) x[8 * i + q] = 0.f;
-              }
+              for (int q = 0; q < 8; ++q) x[8 * i + q] = 0.f;
             }
           }
           mbar_arrive(&sm.raw_free[s]);  // this thread is done with the raw stage
-          if constexpr (ROPE) {
-            if (!is_v) {
-#pragma unroll
-              for (int i = 0; i < 2; ++i)
-                if (r0k + 32 * i < nv) {
-#pragma unroll
-                  for (int e = 0; e < 8; e += 2) {
-                    const float4 cs = kcs[i][e >> 1];  // (cos, sin) of pairs 8c+e, 8c+e+1
-                    rot(x[16 * i + e], x[16 * i + e + 8], cs.x, cs.y);
-                    rot(x[16 * i + e + 1], x[16 * i + e + 9], cs.z, cs.w);
-                  }
-                }
-            }
-          }
           float fm = 0.f;
 #pragma unroll
           for (int q = 0; q < 32; ++q) fm = fmaxf(fm, fabsf(x[q]));
           mx = __float_as_uint(fm);  // (a NaN drops out of the max; it still propagates through the products)
         }
         // The operand stage is free once the products of tile g-3 are complete.
-        if (w && g >= kOpStages)
-          w = wait(is_v ? &sm.v_free[s] : &sm.k_free[s], static_cast<uint32_t>((g - kOpStages) / kOpStages) & 1u);
+        if (w && g >= kOpStages) w = wait(&freed[s], static_cast<uint32_t>((g - kOpStages) / kOpStages) & 1u);
         mx = __reduce_max_sync(0xffffffffu, mx);
         if (lane == 0) sm.red[is_v][par][gw] = mx;
         if (bar_any(gbar, kGroupThreads, !w)) { ok = false; break; }  // also publishes red[][par]
         mx = max(max(sm.red[is_v][par][0], sm.red[is_v][par][1]), max(sm.red[is_v][par][2], sm.red[is_v][par][3]));
         const int e2 = scale_exp(mx);
         const float sc = pow2(e2);
-        const uint32_t oh = smem_addr(&sm.op[s][is_v ? kOpVh : kOpKh][0]);
-        const uint32_t ol = smem_addr(&sm.op[s][is_v ? kOpVl : kOpKl][0]);
-        if (!is_v) {
+        const uint32_t oh = smem_addr(&sm.op[s][op_h][0]), ol = oh + kOpElems * 2;
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            uint32_t h[8], l[8];
+        for (int i = 0; i < 4; ++i) {
+          uint32_t h[4], l[4];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) split2(x[16 * i + 2 * e] * sc, x[16 * i + 2 * e + 1] * sc, h[e], l[e]);
-            const uint32_t o = static_cast<uint32_t>(i * 32 * 128);
-            sts128u(oh + kop_a + o, h[0], h[1], h[2], h[3]);
-            sts128u(oh + kop_b + o, h[4], h[5], h[6], h[7]);
-            sts128u(ol + kop_a + o, l[0], l[1], l[2], l[3]);
-            sts128u(ol + kop_b + o, l[4], l[5], l[6], l[7]);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint32_t h[4], l[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) split2(x[8 * i + 2 * e] * sc, x[8 * i + 2 * e + 1] * sc, h[e], l[e]);
-            const uint32_t o = static_cast<uint32_t>(i * 16 * 128);
-            sts128u(oh + vop + o, h[0], h[1], h[2], h[3]);
-            sts128u(ol + vop + o, l[0], l[1], l[2], l[3]);
-          }
+          for (int e = 0; e < 4; ++e) split2(x[8 * i + 2 * e] * sc, x[8 * i + 2 * e + 1] * sc, h[e], l[e]);
+          const uint32_t o = static_cast<uint32_t>(i * 16 * 128);
+          sts128u(oh + oop + o, h[0], h[1], h[2], h[3]);
+          sts128u(ol + oop + o, l[0], l[1], l[2], l[3]);
         }
         fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
         if (gt == 0) {
-          if (is_v) {
-            sm.vfac[g % kMeta] = pow2(-e2);
-            mbar_arrive(&sm.vmeta[g % kMeta]);
-          } else {
-            sm.kfac[g % kMeta] = pow2(-e2);
-            mbar_arrive(&sm.kmeta[g % kMeta]);
-          }
+          fac[g % kMeta] = pow2(-e2);
+          mbar_arrive(&meta[g % kMeta]);
         }
-        mbar_arrive(is_v ? &sm.v_ready[s] : &sm.k_ready[s]);
+        mbar_arrive(&ready[s]);
         if constexpr (TIMED) c_a += static_cast<unsigned long long>(clock64() - c_k0);
       }
     }
