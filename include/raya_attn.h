@@ -42,8 +42,10 @@ typedef enum {
   RAYA_ATTN_ERR_LENGTH = 2,      /* KernelError::Length { name, got, expected } */
   RAYA_ATTN_ERR_UNSUPPORTED = 3, /* KernelError::Unsupported */
   RAYA_ATTN_ERR_CUDA = 4,        /* a CUDA runtime call failed */
-  RAYA_ATTN_ERR_TIMEOUT = 5,     /* a device-side wait gave up (bounded spin) */
-  RAYA_ATTN_ERR_NCCL = 6         /* reserved for collective failures */
+  RAYA_ATTN_ERR_TIMEOUT = 5      /* a device-side wait gave up (bounded spin) */
+  /* The library runs no collective: raya_attn_forward_multi_gpu moves data
+   * with peer copies (failures: RAYA_ATTN_ERR_CUDA), and the NCCL gather of
+   * sharded outputs belongs to the caller's process group. */
 } raya_attn_status;
 
 /* Mask kinds (attention.rs:22-35, generalised):
