@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       float fm = 0.f;
-#pragma unroll
+#pragma unroll 1
       for (int p = 0; p < 2; ++p) {
         float x[16], y[16];
         piece(p, x, y);
@@ -458,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t qh = tmem + lane_off + col_qh(qb);
-#pragma unroll
+#pragma unroll 1
       for (int p = 0; p < 2; ++p) {
         float x[16], y[16];
         piece(p, x, y);
@@ -516,22 +516,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float mult = fmaxf(qmul * sm.kfac[g % kMeta], 1.17549435e-38f);
         const bool full = rlo <= kt && rhi >= kt + kBN;
         const uint32_t sa = tmem + lane_off + col_s(pb);
-        float mraw;
-        {  // pass 1 over S(g): the row max (masked keys -inf)
-          float sv[64];
-          tmem_ld32(sa, sv);
-          tmem_ld32(sa + 32, sv + 32);
+        float mraw = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {  // pass 1 over S(g), 16 columns at a time: the row max (masked keys -inf)
+          float s16[16];
+          tmem_ld16(sa + 16 * c, s16);
           if (!full) {
 #pragma unroll
-            for (int c = 0; c < 64; ++c)
-              if (static_cast<unsigned>(kt + c - rlo) >= static_cast<unsigned>(rhi - rlo)) sv[c] = -INFINITY;
+            for (int i = 0; i < 16; ++i)
+              if (static_cast<unsigned>(kt + 16 * c + i - rlo) >= static_cast<unsigned>(rhi - rlo)) s16[i] = -INFINITY;
           }
-          float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
+          float m4[4] = {s16[0], s16[1], s16[2], s16[3]};
 #pragma unroll
-          for (int c = 4; c < 64; c += 8)
+          for (int i = 4; i < 16; i += 8)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) m4[q] = fmax3(m4[q], sv[c + q], sv[c + 4 + q]);
-          mraw = fmax3(fmaxf(m4[0], m4[1]), m4[2], m4[3]);
+            for (int q = 0; q < 4; ++q) m4[q] = fmax3(m4[q], s16[i + q], s16[i + 4 + q]);
+          mraw = fmax3(mraw, fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         }
         const float mc = mraw * mult;
         float alpha = 1.f;
@@ -587,28 +587,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (__any_sync(0xffffffffu, !w)) { ok = false; break; }
           tc_fence_after();
           const float vf = sm.vfac[gp % kMeta];
-          const bool rescale = __any_sync(0xffffffffu, alpha != 1.f);
           float tt[64];
           tmem_ld32(tmem + lane_off + col_o(gp & 1), tt);
           tmem_ld32(tmem + lane_off + col_o(gp & 1) + 32, tt + 32);
           tc_fence_before();
           mbar_arrive(&sm.o_free[gp & 1]);  // PV(g+1) may overwrite this partial
           const float2 vf2 = make_float2(vf, vf), al2 = make_float2(alpha, alpha);
-          if (rescale) {
 #pragma unroll
-            for (int i = 0; i < 64; i += 2) {
-              const float2 r =
-                  __fmul2_rn(__ffma2_rn(make_float2(tt[i], tt[i + 1]), vf2, make_float2(o[i], o[i + 1])), al2);
-              o[i] = r.x;
-              o[i + 1] = r.y;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 64; i += 2) {
-              const float2 r = __ffma2_rn(make_float2(tt[i], tt[i + 1]), vf2, make_float2(o[i], o[i + 1]));
-              o[i] = r.x;
-              o[i + 1] = r.y;
-            }
+          for (int i = 0; i < 64; i += 2) {  // (O + t) * alpha, with alpha == 1 exact when the max is kept
+            const float2 r =
+                __fmul2_rn(__ffma2_rn(make_float2(tt[i], tt[i + 1]), vf2, make_float2(o[i], o[i + 1])), al2);
+            o[i] = r.x;
+            o[i + 1] = r.y;
           }
         }
         if constexpr (TIMED) c_a += static_cast<unsigned long long>(clock64() - c_s0);
@@ -692,29 +682,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (TIMED) c_k0 = clock64();
         const int kt = (u.t_begin + t) * kBN;
         const int nv = min(kBN, u.valid - kt);  // valid rows of this tile (>= 1)
-        float x[32];
         uint32_t mx = 0;
         bool w = wait(&sm.raw_full[s], static_cast<uint32_t>(g / kRawStages) & 1u);
-        if (w) {
-          const uint32_t base = smem_addr(&sm.raw[s][is_v ? 1 : 0][0][0][0]);
+        const uint32_t base = smem_addr(&sm.raw[s][is_v ? 1 : 0][0][0][0]);
+        // unit i's 8 elements (zeros for keys at or past valid_len)
+        auto unit_x = [&](int i, float* e) {
+          if (r0s + 16 * i < nv) {
+            const uint32_t o = static_cast<uint32_t>(i * 16 * 128);
+            const float4 x0 = lds128(base + off0 + o), x1 = lds128(base + off1 + o);
+            e[0] = x0.x; e[1] = x0.y; e[2] = x0.z; e[3] = x0.w; e[4] = x1.x; e[5] = x1.y; e[6] = x1.z; e[7] = x1.w;
+          } else {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            if (r0s + 16 * i < nv) {
-              const uint32_t o = static_cast<uint32_t>(i * 16 * 128);
-              const float4 x0 = lds128(base + off0 + o), x1 = lds128(base + off1 + o);
-              float* e = x + 8 * i;
-              e[0] = x0.x; e[1] = x0.y; e[2] = x0.z; e[3] = x0.w; e[4] = x1.x; e[5] = x1.y; e[6] = x1.z;
-              e[7] = x1.w;
-            } else {  // keys at or past valid_len: exact zeros
-#pragma unroll
-              for (int q = 0; q < 8; ++q) x[8 * i + q] = 0.f;
-            }
+            for (int q = 0; q < 8; ++q) e[q] = 0.f;
           }
-          mbar_arrive(&sm.raw_free[s]);  // this thread is done with the raw stage
+        };
+        if (w) {  // pass 1: the largest magnitude (a NaN drops out of the max; it still propagates)
           float fm = 0.f;
+#pragma unroll 1
+          for (int i = 0; i < 4; ++i) {
+            float e[8];
+            unit_x(i, e);
 #pragma unroll
-          for (int q = 0; q < 32; ++q) fm = fmaxf(fm, fabsf(x[q]));
-          mx = __float_as_uint(fm);  // (a NaN drops out of the max; it still propagates through the products)
+            for (int q = 0; q < 8; ++q) fm = fmaxf(fm, fabsf(e[q]));
+          }
+          mx = __float_as_uint(fm);
         }
         // The operand stage is free once the products of tile g-3 are complete.
         if (w && g >= kOpStages) w = wait(&freed[s], static_cast<uint32_t>((g - kOpStages) / kOpStages) & 1u);
@@ -725,15 +716,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int e2 = scale_exp(mx);
         const float sc = pow2(e2);
         const uint32_t oh = smem_addr(&sm.op[s][op_h][0]), ol = oh + kOpElems * 2;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
+#pragma unroll 1
+        for (int i = 0; i < 4; ++i) {  // pass 2: reload, scale, split, store
+          float x[8];
+          unit_x(i, x);
           uint32_t h[4], l[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) split2(x[8 * i + 2 * e] * sc, x[8 * i + 2 * e + 1] * sc, h[e], l[e]);
+          for (int e = 0; e < 4; ++e) split2(x[2 * e] * sc, x[2 * e + 1] * sc, h[e], l[e]);
           const uint32_t o = static_cast<uint32_t>(i * 16 * 128);
           sts128u(oh + oop + o, h[0], h[1], h[2], h[3]);
           sts128u(ol + oop + o, l[0], l[1], l[2], l[3]);
         }
+        mbar_arrive(&sm.raw_free[s]);  // this thread is done with the raw stage
         fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
         if (gt == 0) {
           fac[g % kMeta] = pow2(-e2);
