@@ -199,20 +199,6 @@ __device__ __forceinline__ void mma_f16_ts_e(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
-// 32 packed 32-bit columns of this thread's lane.
-__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
-  tc32::tmem_st32(taddr, reinterpret_cast<const float*>(v));
-}
-// 16 packed 32-bit columns of this thread's lane; completion is awaited by
-// tmem_wait_st.
-__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-      "%14, %15, %16};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
-}
 // 8 packed 32-bit columns of this thread's lane; completion is awaited by
 // tmem_wait_st.
 __device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* v) {
