@@ -92,3 +92,51 @@ def test_relative_error_at_the_1e3_floor(cuda_device, name, picks):
           f"floor 1e-2: GPU {worst['gpu'][1e-2]:.3e}, Tiled {worst['tiled'][1e-2]:.3e}")
     assert worst["gpu"][1e-3] <= 2.0 * worst["tiled"][1e-3]
     assert worst["gpu"][1e-2] < 1e-4
+
+
+SCALES = [(1.0, 1.0, 1.0), (1e3, 1e-3, 1e5), (1e-4, 1e4, 1e-6), (3e4, 1e-4, 7e4), (2.0 ** -20, 2.0 ** 20, 2.0 ** 30)]
+
+
+@pytest.mark.parametrize("kernel", [rb.KERNEL_AUTO, rb.KERNEL_TC32_WS, rb.KERNEL_TC32_WS2, rb.KERNEL_TC16_WS,
+                                    rb.KERNEL_TC16_WS2])
+@pytest.mark.parametrize("sq,sk,sv", SCALES, ids=[f"q{a:g}-k{b:g}-v{c:g}" for a, b, c in SCALES])
+def test_operand_magnitudes(cuda_device, kernel, sq, sk, sv):
+    """q, k and v far from unit size, past fp16's range (65504) and below its
+    normal range (6.1e-5): the 3xFP16 kernel scales each q row and each
+    64-key K and V tile by a power of two, the 3xTF32 kernel needs none.  The
+    scores are the same as at unit size (sq * sk = 1 for all but the last
+    case), so the error is measured relative to the scale of V."""
+    p = oracle.Problem(2, 2, 700, 64, mask=oracle.MASK_BLOCK, block=128, halo=1)
+    q, k, v = oracle.qkv(p.numel, 77)
+    q, k, v = ((x.astype(np.float64) * s).astype(np.float32) for x, s in ((q, sq), (k, sk), (v, sv)))
+    valid = [700, 411]
+    got = cuda_device_run(p, q, k, v, valid=valid, kernel=kernel).astype(np.float64)
+    want = oracle.dense_reference(p, q, k, v, np.array(valid, dtype=np.int32))
+    err = float(np.abs(got - want).max()) / sv
+    assert err < ATOL, f"kernel {kernel}, scales ({sq:g}, {sk:g}, {sv:g}): max abs / |v| {err:.3e}"
+
+
+@pytest.mark.parametrize("kernel", [rb.KERNEL_TC32_WS2, rb.KERNEL_TC16_WS, rb.KERNEL_TC16_WS2])
+def test_magnitudes_varying_by_key_tile(cuda_device, kernel):
+    """Operand sizes that change by 2^20 to 2^40 from one 64-key tile to the
+    next (so every K and V tile of the 3xFP16 kernel gets its own scale, V
+    tiles beyond fp16's range) and q rows whose size falls by 2^20 along the
+    sequence.  The scores stay O(1), so fp32 arithmetic gives ~1e-7 of the
+    largest |V|; the outputs must match fp64 to the parity bar on that scale."""
+    p = oracle.Problem(1, 2, 640, 64, mask=oracle.MASK_FULL)
+    q, k, v = oracle.qkv(p.numel, 91)
+    pos = np.arange(p.seq)
+    even = (pos // 64) % 2 == 0
+    row_scale = 2.0 ** (-20.0 * pos / p.seq)          # per query row: 1 .. 2^-20
+    k_scale = np.where(even, 1.0, 2.0 ** -20)          # per key tile
+    v_scale = np.where(even, 2.0 ** 20, 2.0 ** -20)    # per key tile
+    shape = (p.batch, p.heads, p.seq, p.head_dim)
+    q = (q.reshape(shape) * row_scale[None, None, :, None]).astype(np.float32).ravel()
+    k = (k.reshape(shape) * k_scale[None, None, :, None]).astype(np.float32).ravel()
+    v = (v.reshape(shape) * v_scale[None, None, :, None]).astype(np.float32).ravel()
+    got = cuda_device_run(p, q, k, v, kernel=kernel).astype(np.float64)
+    want = oracle.dense_reference(p, q, k, v, np.full(p.batch, p.seq, dtype=np.int32))
+    # each output row is a convex combination of V rows: its error scale is max |V|
+    vmax = float(np.abs(v).max())
+    err = float(np.abs(got - want).max()) / vmax
+    assert err < ATOL, f"kernel {kernel}: max abs / max|v| {err:.3e}"
