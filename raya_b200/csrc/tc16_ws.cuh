@@ -164,12 +164,6 @@ __device__ __forceinline__ void split2(float e0, float e1, uint32_t& h, uint32_t
   const float2 lo = __ffma2_rn(make_float2(h0, h1), make_float2(-1.f, -1.f), make_float2(e0, e1));
   l = pack_f16x2(lo.x, lo.y);
 }
-// max of three floats in one instruction.
-__device__ __forceinline__ float fmax3(float x, float y, float z) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(x), "f"(y), "f"(z));
-  return r;
-}
 // 16 consecutive fp32 columns of this thread's TMEM lane (load and wait in
 // one statement).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
@@ -512,12 +506,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 16; ++i)
               if (static_cast<unsigned>(kt + 16 * c + i - rlo) >= static_cast<unsigned>(rhi - rlo)) s16[i] = -INFINITY;
           }
-          float m4[4] = {s16[0], s16[1], s16[2], s16[3]};
+          // Chain q takes columns q, q + 4, q + 8, q + 12.
+          float m4[4];
 #pragma unroll
-          for (int i = 4; i < 16; i += 8)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) m4[q] = fmax3(m4[q], s16[i + q], s16[i + 4 + q]);
-          mraw = fmax3(mraw, fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+          for (int q = 0; q < 4; ++q) m4[q] = tc32::fmax3(s16[q], s16[4 + q], fmaxf(s16[8 + q], s16[12 + q]));
+          mraw = tc32::fmax3(mraw, fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         }
         const float mc = mraw * mult;
         float alpha = 1.f;

@@ -84,6 +84,22 @@ __device__ __forceinline__ float tf32_lo(float x) {
   return __fsub_rn(x, __uint_as_float(__float_as_uint(x) & 0xFFFFE000u));
 }
 
+// x - trunc(x) for a pair, in place (one packed FMA: x - hi is exact).
+__device__ __forceinline__ void tf32_lo2(float& x, float& y) {
+  const float2 hi = make_float2(__uint_as_float(__float_as_uint(x) & 0xFFFFE000u),
+                                __uint_as_float(__float_as_uint(y) & 0xFFFFE000u));
+  const float2 lo = __ffma2_rn(hi, make_float2(-1.f, -1.f), make_float2(x, y));
+  x = lo.x;
+  y = lo.y;
+}
+
+// max of three floats in one instruction.
+__device__ __forceinline__ float fmax3(float x, float y, float z) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(x), "f"(y), "f"(z));
+  return r;
+}
+
 // Byte offset of 16-byte chunk c4 (columns 4c4..4c4+3) of row r in a
 // 128-byte-swizzled [ROWS][64] tile held as two column halves of [ROWS][32].
 template <int ROWS>

@@ -345,9 +345,14 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         for (int c = 0; c < 64; ++c)
           if (static_cast<unsigned>(kt + c - rlo) >= static_cast<unsigned>(rhi - rlo)) sv[c] = -INFINITY;
       }
-      float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
+      // Four chains; chain q takes columns q, q + 4, ..., q + 60.
+      float m4[4];
 #pragma unroll
-      for (int c = 4; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], sv[c]);
+      for (int q = 0; q < 4; ++q) m4[q] = fmaxf(sv[q], sv[4 + q]);
+#pragma unroll
+      for (int c = 8; c < 64; c += 8)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) m4[q] = fmax3(m4[q], sv[c + q], sv[c + 4 + q]);
       const float mc = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * qscale;
       // Move the running max only when it grows by more than 2^8 (or is
       // first set): O and l are then rescaled by alpha; otherwise weights
@@ -358,15 +363,16 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         m_used = mc;
       }
       const float mbase = m_used == -INFINITY ? 0.f : m_used;
-      float rs = 0.f;
+      float2 rs2 = make_float2(0.f, 0.f);
+      const float2 qs2 = make_float2(qscale, qscale), nb2 = make_float2(-mbase, -mbase);
 #pragma unroll
-      for (int c = 0; c < 64; c += 4) {
-        sv[c] = ex2(fmaf(sv[c], qscale, -mbase));
-        sv[c + 1] = ex2(fmaf(sv[c + 1], qscale, -mbase));
-        sv[c + 2] = ex2(fmaf(sv[c + 2], qscale, -mbase));
-        sv[c + 3] = ex2(fmaf(sv[c + 3], qscale, -mbase));
-        rs += (sv[c] + sv[c + 1]) + (sv[c + 2] + sv[c + 3]);
+      for (int c = 0; c < 64; c += 2) {
+        const float2 arg = __ffma2_rn(make_float2(sv[c], sv[c + 1]), qs2, nb2);
+        sv[c] = ex2(arg.x);
+        sv[c + 1] = ex2(arg.y);
+        rs2 = __fadd2_rn(rs2, make_float2(sv[c], sv[c + 1]));
       }
+      const float rs = rs2.x + rs2.y;
       lsum = fmaf(lsum, alpha, rs);
 
       if (j >= 2) {  // P buffer pb is free once PV(j-2) is complete
@@ -380,7 +386,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       tmem_st32(ph, sv);
       tmem_st32(ph + 32, sv + 32);
 #pragma unroll
-      for (int c = 0; c < 64; ++c) sv[c] = tf32_lo(sv[c]);
+      for (int c = 0; c < 64; c += 2) tf32_lo2(sv[c], sv[c + 1]);
       tmem_st32(ph + 64, sv);
       tmem_st32(ph + 96, sv + 32);
       if (j > 0) {
@@ -396,11 +402,20 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           float t[32];
           tmem_ld32(tmem + lane_off + kWsColO + c, t);
           if (rescale) {
+            const float2 al2 = make_float2(alpha, alpha);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[c + i] = __fmul_rn(__fadd_rn(o[c + i], t[i]), alpha);
+            for (int i = 0; i < 32; i += 2) {
+              const float2 r = __fmul2_rn(__fadd2_rn(make_float2(o[c + i], o[c + i + 1]), make_float2(t[i], t[i + 1])), al2);
+              o[c + i] = r.x;
+              o[c + i + 1] = r.y;
+            }
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[c + i] = __fadd_rn(o[c + i], t[i]);
+            for (int i = 0; i < 32; i += 2) {
+              const float2 r = __fadd2_rn(make_float2(o[c + i], o[c + i + 1]), make_float2(t[i], t[i + 1]));
+              o[c + i] = r.x;
+              o[c + i + 1] = r.y;
+            }
           }
         }
       }
