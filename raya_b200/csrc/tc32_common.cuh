@@ -177,10 +177,12 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
                "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z), "r"(w)
                : "memory");
 }
-// Commits the issuing thread's bulk stores and waits until their shared-memory
-// sources have been read (the global writes complete on their own).
-__device__ __forceinline__ void tma_store_commit_and_wait_read() {
-  asm volatile("cp.async.bulk.commit_group;\n\tcp.async.bulk.wait_group.read 0;" ::: "memory");
+// Commits the issuing thread's bulk stores as one group.
+__device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the issuing thread's committed bulk stores have read their
+// shared-memory sources (the global writes complete on their own).
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 // Tensor maps of the two-issuer kernels.
