@@ -254,15 +254,18 @@ def l2_note(nbytes: float) -> str:
 
 # ---------------------------------------------------------------- B200 arm
 
-def kernel_label(rb, chosen, shape, packed) -> str:
+def kernel_label(rb, chosen, shape, packed, block) -> str:
+    # (the row tiles per CTA of kernel 37 follow raya_attn.cu's rule)
     if chosen == rb.KERNEL_ROWWISE:
         return "rowwise (raya_b200/csrc/rowwise.cuh)"
     if chosen == rb.KERNEL_TC32_WS:
         return ("tc32_ws, two MMA-issuing warps, PV summed in fp32 registers, 3xTF32 tcgen05 "
                 "(raya_b200/csrc/tc32_ws.cuh), kernel id 34")
     if chosen == rb.KERNEL_TC32_WS2:
-        return (("tc32_ws with four 128-row tiles (a whole slice) per CTA" if (shape.seq + 127) // 128 == 4
-                 and not packed else "tc32_ws with two 128-row tiles per CTA")
+        tiles = (shape.seq + 127) // 128
+        many = tiles % 4 == 0 and block >= 128 and shape.batch * shape.heads * tiles >= 16384
+        units = "four 128-row tiles (a whole slice)" if tiles == 4 else "four 128-row tiles" if many else "two 128-row tiles"
+        return (f"tc32_ws with {'two 128-row tiles' if packed else units} per CTA"
                 + " (raya_b200/csrc/tc32_ws.cuh), kernel id 37")
     if chosen == rb.KERNEL_TC16_WS:
         return ("tc16_ws, 3xFP16 tcgen05 kind::f16 with power-of-two operand scaling, two MMA-issuing warps, "
@@ -507,7 +510,7 @@ def run_b200(args) -> None:
         "gpu_launches": args.steps * w.layers,
         "layout": ("packed qkv -> context" + (f", rope theta {args.rope_theta:g}" if args.rope_theta else "")
                    if args.packed else "head-major q, k, v -> out"),
-        "kernel": kernel_label(rb, chosen, shape, args.packed),
+        "kernel": kernel_label(rb, chosen, shape, args.packed, w.block),
         "kernel_choice": "automatic (raya_attn_kernel_for)" if args.kernel == rb.KERNEL_AUTO else "--kernel",
         "roofline": roofline, "e2e": e2e, "gather": gather, "cpu_baseline": cpu, "clocks": clocks,
         "stages": stages,

@@ -105,9 +105,11 @@ typedef enum {
   RAYA_KERNEL_TC32_WS = 34,
   /* RAYA_KERNEL_TC32_WS with two 128-row tiles per CTA (four where a
    * (batch, head) slice is four row tiles, seq 385..512, so that a CTA runs
-   * the whole slice; head-major layout), one after the other, each run as a
-   * CTA of its own (sharing only the CTA's launch, tensor-memory allocation
-   * and valid_len loads). */
+   * the whole slice, and where the slice's row tiles are a multiple of four
+   * under a block mask of 128 keys or more, with at least 16384 row tiles in
+   * all; head-major layout), one after
+   * the other, each run as a CTA of its own (sharing only the CTA's launch,
+   * tensor-memory allocation and valid_len loads). */
   RAYA_KERNEL_TC32_WS2 = 37,
   /* The same pipeline on tcgen05 kind::f16 in 3xFP16: each fp32 operand is
    * scaled by a power of two (per q row, per 64-key K or V tile) so that its

@@ -462,9 +462,14 @@ raya_attn_status launch_on(DeviceCtx* ctx, const raya_attn_desc* d, const float*
       return fail(RAYA_ATTN_ERR_UNSUPPORTED, "unsupported: %llu rows exceed the tensor-map row limit",
                   static_cast<unsigned long long>(rows));
     {
-      // UNITS row tiles per CTA: 1 (kernel 34), 4 where a slice is four row
-      // tiles, else 2 (kernel 37); the stage-timing build where asked.
-      const int units = kernel_id == RAYA_KERNEL_TC32_WS ? 1 : a.row_tiles == 4 ? 4 : 2;
+      // UNITS row tiles per CTA: 1 (kernel 34); for kernel 37 4 where a slice
+      // is four row tiles, or a multiple of four with blocks of 128 keys or
+      // more and at least 16384 row tiles in all (c5: +0.7% over 2, same box;
+      // c3 at 3072 row tiles -3 to -4%: a partial last wave of 768 CTAs;
+      // c2's 64-key blocks -1.2%), else 2; the stage-timing build where asked.
+      const bool four = a.row_tiles == 4 || (a.row_tiles % 4 == 0 && d->mask == RAYA_MASK_BLOCK &&
+                                             d->block >= 128 && grid >= 16384);
+      const int units = kernel_id == RAYA_KERNEL_TC32_WS ? 1 : four ? 4 : 2;
       using WsFn = void (*)(AttnArgs, tc32::PipeMaps);
       WsFn fn = nullptr;
       if (units == 1)
